@@ -1,0 +1,553 @@
+"""Benchmark of the causal conv1d hot path on B200 (one JSON line).
+
+Headline workload ("C2"): Mamba-2 2.7B-style
+prefill, causal_conv1d_fn forward + backward, bf16, x (8, 5376, 2048) in
+channel-last strides, width 4, bias, SiLU, initial_states and
+return_final_states, grad_out ~ N(0,1).  One step = forward + backward of
+one batch; with N GPUs every rank runs its own batch of 8 (global batch 8N,
+weak scaling) and the fp32 [dweight | dbias] partials are summed with one
+NCCL all-reduce.
+
+  value  -- whole-job tokens/s on device-resident inputs (CUDA events, max
+            over ranks); inputs (176 MB per tensor) are larger than L2.
+  e2e    -- the same step through the public API from pinned HOST buffers:
+            host->device copies of the step's inputs and device->host reads
+            of all its outputs inside the timed region.
+  roofline / kernels -- algorithmic HBM bytes / CUDA-event kernel time per
+            op (fwd, bwd, decode update C3a/C3b, varlen C4, large C5) against
+            the measured copy bandwidth of MEASURED_PEAKS.json.
+  cpu_baseline -- the reference's CPU algorithm (C restatement in oracle/,
+            all host threads) on a bounded sample of the same workload.
+
+`--impl reference` times that CPU path alone as the reference arm.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+REPO = Path(__file__).resolve().parent
+sys.path[:0] = [str(REPO / "causal-conv1d-mojo_b200"), str(REPO)]
+
+import torch  # noqa: E402
+
+METRIC = "fwd/bwd/update HBM GB/s vs B200 peak; tokens/s at 1/2/4/8 B200"
+UNIT = "tokens/s"
+B, D, L, W = 8, 5376, 2048, 4
+DT = torch.bfloat16
+ESZ = 2
+
+FALLBACK_HBM_GBS = 6650.0
+
+
+def peaks():
+    p = REPO / "MEASURED_PEAKS.json"
+    if p.is_file():
+        d = json.loads(p.read_text())
+        return float(d["hbm_gbs"]), "measured"
+    return FALLBACK_HBM_GBS, "fallback"
+
+
+def c2_bytes():
+    n = B * D * L
+    states = B * D * (W - 1) * ESZ
+    wb = D * (W + 1) * ESZ
+    fwd = 2 * n * ESZ + 2 * states + wb  # x, out, init, final, w/b
+    bwd = 3 * n * ESZ + 2 * states + wb + D * (W + 1) * 4 + wb  # x, dout, dx, init, dinit, w/b, fp32 dw|db, dtype dw|db
+    return fwd, bwd
+
+
+# --------------------------------------------------------------------------
+# clocks sampler (nvidia-smi during the timed region)
+# --------------------------------------------------------------------------
+
+class Clocks:
+    FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
+              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+              "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.index = index
+        self.samples = []
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except (OSError, ValueError):
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) == 7:
+                self.samples.append(parts)
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+        return False
+
+    def summary(self):
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+        sm = sorted(float(s[0]) for s in self.samples if s[0].replace(".", "").isdigit())
+        mx = [float(s[1]) for s in self.samples if s[1].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for s in self.samples for i in range(4) if s[3 + i] == "Active"})
+        return {"sm_mhz": sm[len(sm) // 2] if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(self.samples)}
+
+
+# --------------------------------------------------------------------------
+# distributed plumbing
+# --------------------------------------------------------------------------
+
+def dist_env():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return world, rank, local
+
+
+def init_dist(world, local):
+    import datetime
+
+    import torch.distributed as dist
+
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    return dist
+
+
+def max_over_ranks(v, world):
+    if world == 1:
+        return v
+    import torch.distributed as dist
+
+    t = torch.tensor([v], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def barrier_sync(world):
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+    torch.cuda.synchronize()
+
+
+# --------------------------------------------------------------------------
+# our arm
+# --------------------------------------------------------------------------
+
+def make_c2(seed, device):
+    g = torch.Generator(device=device).manual_seed(seed)
+
+    def nrm(*s):
+        return torch.randn(*s, generator=g, device=device, dtype=torch.float32).to(DT)
+
+    def uni(*s):
+        return (torch.rand(*s, generator=g, device=device, dtype=torch.float32) - 0.5).to(DT)
+
+    x = nrm(B, L, D).transpose(1, 2)
+    w = uni(D, W)
+    b = uni(D)
+    init = nrm(B, D, W - 1)
+    dout = nrm(B, L, D).transpose(1, 2)
+    return x, w, b, init, dout
+
+
+def time_c2(args, world, rank):
+    from causal_conv1d_b200 import _ops
+    from causal_conv1d_b200.parallel import allreduce_weight_grads, split_dwdb
+
+    x, w, b, init, dout = make_c2(1234 + rank, "cuda")
+    out = torch.empty_like(x)
+    fs = torch.empty(B, D, W - 1, dtype=DT, device="cuda")
+    dx = torch.empty_like(x)
+    dwdb = torch.empty(D * (W + 1), dtype=torch.float32, device="cuda")
+    dw = torch.empty(D, W, dtype=DT, device="cuda")
+    db = torch.empty(D, dtype=DT, device="cuda")
+    dinit = torch.empty_like(init)
+    K = args.steps
+    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(K)]
+
+    def step(e=None):
+        if e is not None:
+            e[0].record()
+        _ops.fwd(x, w, b, None, init, out, True, fs)
+        if e is not None:
+            e[1].record()
+        if world > 1:
+            _ops.bwd(x, w, b, dout, None, init, None, dx, dwdb, dinit, None, None, True)
+            if e is not None:
+                e[2].record()
+            allreduce_weight_grads(dwdb)
+            gw, gb = split_dwdb(dwdb, D, W)
+            dw.copy_(gw)
+            db.copy_(gb)
+        else:
+            _ops.bwd(x, w, b, dout, None, init, None, dx, dwdb, dinit, dw, db, True)
+            if e is not None:
+                e[2].record()
+
+    for _ in range(args.warmup):
+        step()
+    barrier_sync(world)
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with Clocks(torch.cuda.current_device()) as clk:
+        start.record()
+        for k in range(K):
+            step(ev[k])
+        stop.record()
+        torch.cuda.synchronize()
+    total_ms = start.elapsed_time(stop)
+    fwd_ms = sum(e[0].elapsed_time(e[1]) for e in ev) / K
+    bwd_ms = sum(e[1].elapsed_time(e[2]) for e in ev) / K
+    barrier_sync(world)
+    total_ms = max_over_ranks(total_ms, world)
+    return dict(ms_per_step=total_ms / K, fwd_ms=fwd_ms, bwd_ms=bwd_ms, clocks=clk.summary())
+
+
+def time_e2e(args, world, rank):
+    """Public API, host buffers in and out, every step."""
+    from causal_conv1d_b200 import causal_conv1d_fn
+    from causal_conv1d_b200.parallel import causal_conv1d_fn_batch_sharded
+
+    xd, wd, bd, initd, doutd = make_c2(99 + rank, "cuda")
+    # Channel-last activations live on the host as (B, L, D) arrays.
+    host = dict(x=xd.transpose(1, 2).contiguous(), w=wd, b=bd, init=initd, dout=doutd.transpose(1, 2).contiguous())
+    host = {k: v.cpu().pin_memory() for k, v in host.items()}
+    del xd, wd, bd, initd, doutd
+    outs = {k: torch.empty(s, dtype=DT).pin_memory() for k, s in dict(
+        out=(B, L, D), fs=(B, D, W - 1), dx=(B, L, D), dw=(D, W), db=(D,), dinit=(B, D, W - 1)).items()}
+    h2d = sum(t.numel() * t.element_size() for t in host.values())
+    d2h = sum(t.numel() * t.element_size() for t in outs.values())
+
+    def step():
+        x = host["x"].to("cuda", non_blocking=True).transpose(1, 2).requires_grad_()
+        w = host["w"].to("cuda", non_blocking=True).requires_grad_()
+        b = host["b"].to("cuda", non_blocking=True).requires_grad_()
+        init = host["init"].to("cuda", non_blocking=True).requires_grad_()
+        dout = host["dout"].to("cuda", non_blocking=True).transpose(1, 2)
+        if world > 1:
+            out, fs = causal_conv1d_fn_batch_sharded(x, w, b, initial_states=init, return_final_states=True,
+                                                      activation="silu")
+        else:
+            out, fs = causal_conv1d_fn(x, w, b, initial_states=init, return_final_states=True, activation="silu")
+        torch.autograd.backward([out], [dout])
+        outs["out"].copy_(out.detach().transpose(1, 2), non_blocking=True)
+        outs["fs"].copy_(fs.detach(), non_blocking=True)
+        outs["dx"].copy_(x.grad.transpose(1, 2), non_blocking=True)
+        outs["dw"].copy_(w.grad, non_blocking=True)
+        outs["db"].copy_(b.grad, non_blocking=True)
+        outs["dinit"].copy_(init.grad, non_blocking=True)
+
+    K = max(3, min(args.steps, 20))
+    for _ in range(max(3, args.warmup)):
+        step()
+    barrier_sync(world)
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record()
+    for _ in range(K):
+        step()
+    stop.record()
+    torch.cuda.synchronize()
+    ms = max_over_ranks(start.elapsed_time(stop), world) / K
+    return dict(value=world * B * L / (ms / 1e3), unit=UNIT, h2d_bytes_per_step=h2d, d2h_bytes_per_step=d2h,
+                ms_per_step=ms, steps=K, path="causal_conv1d_fn + autograd backward, pinned host buffers")
+
+
+def _kernel_ms(fn, iters, sets):
+    """Average CUDA-event time of fn(i) cycling over `sets` buffer sets."""
+    for i in range(3):
+        fn(i % sets)
+    torch.cuda.synchronize()
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(iters)]
+    for i, (a, c) in enumerate(evs):
+        a.record()
+        fn(i % sets)
+        c.record()
+    torch.cuda.synchronize()
+    return sum(a.elapsed_time(c) for a, c in evs) / iters
+
+
+def time_kernels(peak):
+    """Secondary kernels of the metric, each timed alone."""
+    from causal_conv1d_b200 import _ops
+
+    res = {}
+    g = torch.Generator(device="cuda").manual_seed(7)
+
+    def rn(*s, dt=DT):
+        return torch.randn(*s, generator=g, device="cuda", dtype=torch.float32).to(dt)
+
+    def ru(*s, dt=DT):
+        return (torch.rand(*s, generator=g, device="cuda", dtype=torch.float32) - 0.5).to(dt)
+
+    # C3a: decode update, indexed pool (512, 5376, 3); rotate 8 sets (> L2).
+    Bu, Du = 256, 5376
+    sets = 8
+    w, b = ru(Du, W), ru(Du)
+    xs = [rn(Bu, Du, 1) for _ in range(sets)]
+    pools = [rn(512, Du, W - 1) for _ in range(sets)]
+    idx = [torch.randperm(512, device="cuda")[:Bu].to(torch.int32) for _ in range(sets)]
+    outs = [torch.empty_like(xs[0]) for _ in range(sets)]
+    ms = _kernel_ms(lambda i: _ops.update(xs[i], pools[i], w, b, None, idx[i], outs[i], True), 50, sets)
+    nbytes = Bu * Du * (2 + 2 + 6 + 6) + Du * (W + 1) * 2 + Bu * 4
+    res["update_c3a_indexed"] = dict(ms=ms, gbs=nbytes / ms / 1e6, frac=nbytes / ms / 1e6 / peak,
+                                     tokens_per_s=Bu / (ms / 1e3), algorithmic_bytes=nbytes)
+    del pools
+    # C3b: circular (256, 5376, 8), cache_seqlens ~ U{0..1023}.
+    states = [rn(Bu, Du, 8) for _ in range(sets)]
+    cache = [torch.randint(0, 1024, (Bu,), device="cuda", dtype=torch.int32) for _ in range(sets)]
+    ms = _kernel_ms(lambda i: _ops.update(xs[i], states[i], w, b, cache[i], None, outs[i], True), 50, sets)
+    nbytes = Bu * Du * (2 + 2 + 6 + 2) + Du * (W + 1) * 2 + Bu * 4
+    res["update_c3b_circular"] = dict(ms=ms, gbs=nbytes / ms / 1e6, frac=nbytes / ms / 1e6 / peak,
+                                      tokens_per_s=Bu / (ms / 1e3), algorithmic_bytes=nbytes)
+    del states, xs, outs
+    torch.cuda.empty_cache()
+
+    # C4: varlen packed prefill fp16 (1, 4096, 65536) channel-last + seq_idx.
+    dt = torch.float16
+    Lv, Dv = 65536, 4096
+    gl = torch.Generator().manual_seed(0)
+    raw = torch.randint(256, 4097, (32,), generator=gl)
+    lens = (raw * Lv // raw.sum()).clamp(min=1)
+    lens[-1] += Lv - lens.sum()
+    seq = torch.repeat_interleave(torch.arange(32, dtype=torch.int32), lens).view(1, Lv).cuda()
+    x = rn(1, Lv, Dv, dt=dt).transpose(1, 2)
+    dout = rn(1, Lv, Dv, dt=dt).transpose(1, 2)
+    wv, bv = ru(Dv, W, dt=dt), ru(Dv, dt=dt)
+    out, dx = torch.empty_like(x), torch.empty_like(x)
+    dwdb = torch.empty(Dv * (W + 1), dtype=torch.float32, device="cuda")
+    dw, db = torch.empty(Dv, W, dtype=dt, device="cuda"), torch.empty(Dv, dtype=dt, device="cuda")
+    n = Lv * Dv
+    ms = _kernel_ms(lambda i: _ops.fwd(x, wv, bv, seq, None, out, True, None), 10, 1)
+    nb = 4 * n + Lv * 4 + Dv * (W + 1) * 2
+    res["fwd_c4_varlen"] = dict(ms=ms, gbs=nb / ms / 1e6, frac=nb / ms / 1e6 / peak, tokens_per_s=Lv / (ms / 1e3),
+                                algorithmic_bytes=nb)
+    ms = _kernel_ms(lambda i: _ops.bwd(x, wv, bv, dout, seq, None, None, dx, dwdb, None, dw, db, True), 10, 1)
+    nb = 6 * n + Lv * 4 + Dv * (W + 1) * 2 * 2 + Dv * (W + 1) * 4
+    res["bwd_c4_varlen"] = dict(ms=ms, gbs=nb / ms / 1e6, frac=nb / ms / 1e6 / peak, tokens_per_s=Lv / (ms / 1e3),
+                                algorithmic_bytes=nb)
+    del x, dout, out, dx
+    torch.cuda.empty_cache()
+
+    # C5: large contiguous (64, 8192, 8192) bf16, width 4, SiLU, states on.
+    B5, D5, L5 = 64, 8192, 8192
+    x = rn(B5, D5, L5)
+    out = torch.empty_like(x)
+    w5, b5 = ru(D5, W), ru(D5)
+    init = rn(B5, D5, W - 1)
+    fs = torch.empty_like(init)
+    n = B5 * D5 * L5
+    ms = _kernel_ms(lambda i: _ops.fwd(x, w5, b5, None, init, out, True, fs), 5, 1)
+    nb = 4 * n + 2 * init.numel() * 2 + D5 * (W + 1) * 2
+    res["fwd_c5_large"] = dict(ms=ms, gbs=nb / ms / 1e6, frac=nb / ms / 1e6 / peak,
+                               tokens_per_s=B5 * L5 / (ms / 1e3), algorithmic_bytes=nb)
+    dout = out  # reuse the buffer as grad_out (values irrelevant for timing)
+    dx = torch.empty_like(x)
+    dwdb = torch.empty(D5 * (W + 1), dtype=torch.float32, device="cuda")
+    dw, db, dinit = torch.empty(D5, W, dtype=DT, device="cuda"), torch.empty(D5, dtype=DT, device="cuda"), \
+        torch.empty_like(init)
+    ms = _kernel_ms(lambda i: _ops.bwd(x, w5, b5, dout, None, init, None, dx, dwdb, dinit, dw, db, True), 5, 1)
+    nb = 6 * n + 2 * init.numel() * 2 + D5 * (W + 1) * (2 + 2 + 4)
+    res["bwd_c5_large"] = dict(ms=ms, gbs=nb / ms / 1e6, frac=nb / ms / 1e6 / peak,
+                               tokens_per_s=B5 * L5 / (ms / 1e3), algorithmic_bytes=nb)
+    del x, out, dx
+    torch.cuda.empty_cache()
+    return res
+
+
+# --------------------------------------------------------------------------
+# CPU path (oracle port): baseline leg and reference arm
+# --------------------------------------------------------------------------
+
+def cpu_sample_step(state):
+    """One sample step of the reference CPU algorithm: forward + backward of
+    batch row 0 of C2 (1, 5376, 2048), float accumulation, all threads."""
+    import oracle
+
+    x, w, b, init, dout = state
+    oracle.fwd(x, w, b, None, init, silu=True, return_final_states=True, acc64=False)
+    oracle.bwd(x, w, dout, b, None, init, None, silu=True, acc64=False)
+
+
+def cpu_setup():
+    import oracle
+
+    oracle.load()
+    g = torch.Generator().manual_seed(0)
+    x = torch.randn(1, L, D, generator=g).to(DT).transpose(1, 2)
+    w = (torch.rand(D, W, generator=g) - 0.5).to(DT)
+    b = (torch.rand(D, generator=g) - 0.5).to(DT)
+    init = torch.randn(1, D, W - 1, generator=g).to(DT)
+    dout = torch.randn(1, L, D, generator=g).to(DT).transpose(1, 2)
+    return (x, w, b, init, dout), oracle.max_threads()
+
+
+def cpu_baseline(budget_s=10.0):
+    state, cores = cpu_setup()
+    cpu_sample_step(state)
+    times = []
+    t_end = time.perf_counter() + budget_s
+    while time.perf_counter() < t_end or len(times) < 3:
+        t0 = time.perf_counter_ns()
+        cpu_sample_step(state)
+        times.append((time.perf_counter_ns() - t0) / 1e9)
+        if len(times) >= 200:
+            break
+    best = min(times)
+    return {"value": L / best, "unit": UNIT, "cores": cores, "kind": "port",
+            "sample": f"C2 batch row 0 (1, {D}, {L}) fwd+bwd, bf16, min of {len(times)} runs "
+                      f"({best * 1e3:.1f} ms each); oracle/cc1d_oracle.c float accumulation, OpenMP"}
+
+
+def run_reference(args):
+    world, rank, _ = dist_env()
+    if rank != 0:
+        return 0
+    state, cores = cpu_setup()
+    for _ in range(args.warmup):
+        cpu_sample_step(state)
+    times = []
+    for _ in range(args.steps):
+        t0 = time.perf_counter_ns()
+        cpu_sample_step(state)
+        times.append((time.perf_counter_ns() - t0) / 1e9)
+    ms = 1e3 * sum(times) / len(times)
+    value = L / (ms / 1e3)
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": "C2 Mamba-2 prefill fwd+bwd (sampled: batch row 0 of 8)", "global_batch": B,
+                   "seq_len": L, "dim": D, "width": W, "layout": "channel-last",
+                   "parallelism": "CPU, OpenMP over (b, c) rows"},
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": cores, "kind": "port",
+                         "sample": f"batch row 0 (1, {D}, {L}) of C2 per step; reference CPU algorithm "
+                                   f"(oracle/cc1d_oracle.c, restating fwd_cpu/bwd_full_cpu kernel.mojo)"},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def load_traffic():
+    p = REPO / "profiles" / "ncu_traffic.json"
+    if p.is_file():
+        try:
+            return json.loads(p.read_text())
+        except ValueError:
+            return {}
+    return {}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--skip-kernels", action="store_true", help="skip the secondary kernel table")
+    ap.add_argument("--skip-e2e", action="store_true")
+    ap.add_argument("--skip-cpu", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        return run_reference(args)
+
+    world, rank, local = dist_env()
+    torch.cuda.set_device(local)
+    dist = init_dist(world, local)
+    peak, peak_kind = peaks()
+    fwd_bytes, bwd_bytes = c2_bytes()
+
+    r = time_c2(args, world, rank)
+    e2e = None if args.skip_e2e else time_e2e(args, world, rank)
+    kernels = None
+    if rank == 0 and not args.skip_kernels:
+        kernels = time_kernels(peak)
+    cpu = None
+    if rank == 0 and world == 1 and not args.skip_cpu:
+        cpu = cpu_baseline()
+    if world > 1:
+        dist.barrier()
+
+    if rank == 0:
+        fwd_gbs = fwd_bytes / r["fwd_ms"] / 1e6
+        bwd_gbs = bwd_bytes / r["bwd_ms"] / 1e6
+        traffic = load_traffic().get("bwd_chan_kernel/C2")
+        ktab = {
+            "fwd_c2": dict(ms=r["fwd_ms"], gbs=fwd_gbs, frac=fwd_gbs / peak, algorithmic_bytes=fwd_bytes),
+            "bwd_c2": dict(ms=r["bwd_ms"], gbs=bwd_gbs, frac=bwd_gbs / peak, algorithmic_bytes=bwd_bytes,
+                           note="bwd kernel + dweight/dbias finalize kernel"),
+        }
+        if kernels:
+            ktab.update(kernels)
+        line = {
+            "metric": METRIC,
+            "value": world * B * L / (r["ms_per_step"] / 1e3),
+            "unit": UNIT,
+            "n_gpus": world,
+            "steps": args.steps,
+            "warmup": args.warmup,
+            "ms_per_step": r["ms_per_step"],
+            "higher_is_better": True,
+            "scaling": "weak",
+            "vs_baseline": None,
+            "dtype": "bf16",
+            "data": "synthetic",
+            "config": {
+                "workload": "C2 Mamba-2 2.7B prefill: causal_conv1d_fn fwd+bwd, bf16, x (8, 5376, 2048) "
+                            "channel-last, width 4, bias, SiLU, initial_states, return_final_states",
+                "global_batch": world * B, "seq_len": L, "dim": D, "width": W,
+                "parallelism": f"batch-sharded x{world}" + (", NCCL all-reduce of fp32 dweight|dbias"
+                                                            if world > 1 else ""),
+                "l2": "inputs larger than L2 (x and grad_out are 176 MB each; L2 is 126 MB)",
+            },
+            "roofline": {
+                "bound": "hbm", "achieved": bwd_gbs, "peak": peak, "unit": "GB/s", "frac": bwd_gbs / peak,
+                "traffic": traffic, "kernel": "bwd (bwd_chan_kernel + finalize_kernel), C2",
+                "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured"
+                else "fallback 6.65 TB/s",
+                "algorithmic_bytes_per_launch": bwd_bytes,
+            },
+            "kernels": ktab,
+            "gpu_launches": 3 * args.steps,
+            "clocks": r["clocks"],
+        }
+        if e2e is not None:
+            line["e2e"] = e2e
+        if cpu is not None:
+            line["cpu_baseline"] = cpu
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    raise SystemExit(main())

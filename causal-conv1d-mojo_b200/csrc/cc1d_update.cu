@@ -1,0 +1,180 @@
+// Decode-step kernel of causal_conv1d_update and the varlen state gather
+// of causal_conv1d_varlen_states, for sm_100a.
+//
+// update_kernel: one thread per (b, c).  Semantics follow the reference
+// CPU kernel (src/causal_conv1d_mojo/update_cpu/kernel.mojo:52-139) and the
+// pure-PyTorch reference (src/causal_conv1d_mojo/reference.py:62-121):
+//   * conv_state_indices[b] < 0: out[b] = 0 and the state row is untouched;
+//     otherwise row conv_state_indices[b] (or b) of conv_state serves b;
+//   * linear mode: window = last W-1 state values, then the new state is
+//     the last state_len values of cat([state, x]);
+//   * circular mode: window = state[(cs-(W-1)+j) mod S], x written at
+//     (cs+i) mod S, cs = cache_seqlens[b] (floor modulo S);
+//   * out[i] = act(bias + sum_k w[k] * window[k]) with the same fp32 tap
+//     order as the forward kernel, so decoding token by token reproduces the
+//     forward pass bit for bit.
+//
+// varlen_states_kernel: one thread per (sequence, slot, channel), channel
+// fastest, so reads of x rows and writes of the (batch, state_len, dim)
+// output storage are both coalesced
+// (src/causal_conv1d_mojo/causal_conv1d_varlen.py:29-61).
+#include "cc1d_dispatch.cuh"
+
+namespace cc1d {
+
+namespace {
+
+template <typename T, int W>
+__global__ void __launch_bounds__(128) update_kernel(const UpdateArgs a) {
+  constexpr int H = W - 1;
+  const i64 cblocks = ceil_div(a.D, (i64)blockDim.x);
+  const i64 b = blockIdx.x / cblocks;
+  const i64 c = (blockIdx.x - b * cblocks) * blockDim.x + threadIdx.x;
+  if (c >= a.D) return;
+  const T* __restrict__ x = static_cast<const T*>(a.x);
+  const T* __restrict__ wt = static_cast<const T*>(a.w);
+  const T* __restrict__ bias = static_cast<const T*>(a.bias);
+  T* __restrict__ out = static_cast<T*>(a.out);
+  T* __restrict__ ob = out + b * a.os_b + c * a.os_c;
+  i64 row = b;
+  if (a.idx != nullptr) {
+    const int r = a.idx[b];
+    // Negative: padding token.  An index past the pool is invalid input; it
+    // is treated like padding instead of touching memory outside conv_state.
+    if (r < 0 || r >= a.state_rows) {
+      for (i64 i = 0; i < a.L; ++i) ob[i * a.os_l] = Cvt<T>::to(0.f);
+      return;
+    }
+    row = r;
+  }
+  T* __restrict__ st = static_cast<T*>(a.state) + row * a.ss_b + c * a.ss_c;
+  const T* __restrict__ xb = x + b * a.xs_b + c * a.xs_c;
+  float wv[W];
+#pragma unroll
+  for (int k = 0; k < W; ++k) wv[k] = Cvt<T>::f(wt[c * a.ws_c + k * a.ws_k]);
+  const float bv = bias ? Cvt<T>::f(bias[c * a.bs]) : 0.f;
+  const i64 S = a.S;
+  float win[W];
+  if (a.cache_seqlens != nullptr) {
+    i64 cs = (i64)a.cache_seqlens[b] % S;
+    if (cs < 0) cs += S;
+    i64 ui = cs - H;
+    if (ui < 0) ui += S;
+#pragma unroll
+    for (int j = 0; j < H; ++j) {
+      win[j] = Cvt<T>::f(st[ui * a.ss_l]);
+      ui = (ui + 1 == S) ? 0 : ui + 1;
+    }
+    for (i64 i = 0; i < a.L; ++i) {
+      const T xv = xb[i * a.xs_l];
+      st[ui * a.ss_l] = xv;
+      ui = (ui + 1 == S) ? 0 : ui + 1;
+      win[H] = Cvt<T>::f(xv);
+      float acc = bv;
+#pragma unroll
+      for (int k = 0; k < W; ++k) acc = fmaf(wv[k], win[k], acc);
+      if (a.silu) acc = silu_f(acc);
+      ob[i * a.os_l] = Cvt<T>::to(acc);
+#pragma unroll
+      for (int k = 0; k < H; ++k) win[k] = win[k + 1];
+    }
+  } else {
+    // History = the last H values of the old state.
+#pragma unroll
+    for (int j = 0; j < H; ++j) win[j] = Cvt<T>::f(st[(S - H + j) * a.ss_l]);
+    // New state = last S values of cat([state, x]); ascending j only reads
+    // positions that are not yet overwritten.
+    for (i64 j = 0; j < S; ++j) {
+      const i64 src = a.L + j;
+      st[j * a.ss_l] = (src < S) ? st[src * a.ss_l] : xb[(src - S) * a.xs_l];
+    }
+    for (i64 i = 0; i < a.L; ++i) {
+      win[H] = Cvt<T>::f(xb[i * a.xs_l]);
+      float acc = bv;
+#pragma unroll
+      for (int k = 0; k < W; ++k) acc = fmaf(wv[k], win[k], acc);
+      if (a.silu) acc = silu_f(acc);
+      ob[i * a.os_l] = Cvt<T>::to(acc);
+#pragma unroll
+      for (int k = 0; k < H; ++k) win[k] = win[k + 1];
+    }
+  }
+}
+
+template <typename T>
+__global__ void varlen_states_kernel(const VarlenArgs a) {
+  const i64 n = a.B * a.S * a.D;
+  for (i64 e = (i64)blockIdx.x * blockDim.x + threadIdx.x; e < n; e += (i64)gridDim.x * blockDim.x) {
+    const i64 c = e % a.D;
+    const i64 bj = e / a.D;
+    const i64 j = bj % a.S;
+    const i64 i = bj / a.S;
+    const i64 beg = a.cu[i];
+    const i64 end = a.cu[i + 1];
+    const i64 start = max(beg, end - a.S);
+    const i64 cnt = end - start;
+    T v = Cvt<T>::to(0.f);
+    const i64 tok = end - a.S + j;
+    if (cnt > 0 && j >= a.S - cnt && tok >= 0 && tok < a.total_tokens)
+      v = static_cast<const T*>(a.x)[tok * a.xs_t + c * a.xs_c];
+    static_cast<T*>(a.st)[i * a.ss_b + c * a.ss_c + j * a.ss_l] = v;
+  }
+}
+
+// Update supports widths 2..9 for every dtype (no lane-vector halo).
+template <typename T, typename F>
+cudaError_t dispatch_update_width(int width, F&& f) {
+  switch (width) {
+    case 2: return f.template operator()<T, 2>();
+    case 3: return f.template operator()<T, 3>();
+    case 4: return f.template operator()<T, 4>();
+    case 5: return f.template operator()<T, 5>();
+    case 6: return f.template operator()<T, 6>();
+    case 7: return f.template operator()<T, 7>();
+    case 8: return f.template operator()<T, 8>();
+    case 9: return f.template operator()<T, 9>();
+    default: return cudaErrorInvalidValue;
+  }
+}
+
+struct LaunchUpdate {
+  const UpdateArgs& a;
+  cudaStream_t stream;
+  template <typename T, int W>
+  cudaError_t operator()() {
+    const int threads = 128;
+    const i64 blocks = ceil_div(a.D, (i64)threads) * a.B;
+    if (blocks > 0x7fffffffLL) return cudaErrorInvalidConfiguration;
+    update_kernel<T, W><<<(unsigned)blocks, threads, 0, stream>>>(a);
+    return cudaGetLastError();
+  }
+};
+
+}  // namespace
+
+cudaError_t launch_update(int dtype, int width, const UpdateArgs& a, cudaStream_t stream) {
+  if (a.B == 0 || a.D == 0) return cudaSuccess;
+  LaunchUpdate f{a, stream};
+  switch (dtype) {
+    case 0: return dispatch_update_width<__half>(width, f);
+    case 1: return dispatch_update_width<__nv_bfloat16>(width, f);
+    case 2: return dispatch_update_width<float>(width, f);
+    default: return cudaErrorInvalidValue;
+  }
+}
+
+cudaError_t launch_varlen_states(int dtype, const VarlenArgs& a, cudaStream_t stream) {
+  const i64 n = a.B * a.S * a.D;
+  if (n == 0) return cudaSuccess;
+  const int threads = 256;
+  const unsigned blocks = (unsigned)std::min<i64>(ceil_div(n, threads), 1 << 20);
+  switch (dtype) {
+    case 0: varlen_states_kernel<__half><<<blocks, threads, 0, stream>>>(a); break;
+    case 1: varlen_states_kernel<__nv_bfloat16><<<blocks, threads, 0, stream>>>(a); break;
+    case 2: varlen_states_kernel<float><<<blocks, threads, 0, stream>>>(a); break;
+    default: return cudaErrorInvalidValue;
+  }
+  return cudaGetLastError();
+}
+
+}  // namespace cc1d

@@ -1,0 +1,194 @@
+/*
+ * cc1d.h -- C ABI of the B200 (sm_100a) causal depthwise conv1d library
+ * (libcc1d_sm100.so).
+ *
+ * The reference (causal-conv1d-mojo) crosses its native boundary with a
+ * positional Python tuple of integers per op: data pointers (0 for an absent
+ * tensor), B/D/L, per-tensor strides in elements, flags, a dtype code and the
+ * caller's CUDA stream.  This header replaces those tuples with one plain C
+ * struct per op.  Every pointer is a device address, every stride is counted
+ * in ELEMENTS (not bytes) and is 64-bit, so tensors with more than 2^31
+ * elements are addressed correctly.
+ *
+ * Conventions shared by every entry point:
+ *   - All work is enqueued on `stream` (a cudaStream_t, may be 0 for the
+ *     legacy default stream) of the CURRENT CUDA device.  No entry point
+ *     synchronises, allocates device memory or keeps state between calls.
+ *   - Return value: CC1D_OK (0) or a CC1D_ERR_* code.  The matching message
+ *     is available from cc1d_last_error() on the calling thread.
+ *   - A tensor with zero elements launches nothing and returns CC1D_OK.
+ *   - dtype codes equal the reference's (_dtype.py:16-20): fp16=0, bf16=1,
+ *     fp32=2.
+ */
+#ifndef CC1D_H_
+#define CC1D_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define CC1D_ABI_VERSION 1
+
+#if defined(__GNUC__)
+#define CC1D_API __attribute__((visibility("default")))
+#else
+#define CC1D_API
+#endif
+
+enum cc1d_dtype { CC1D_F16 = 0, CC1D_BF16 = 1, CC1D_F32 = 2 };
+
+enum cc1d_status {
+  CC1D_OK = 0,
+  CC1D_ERR_INVALID_ARGUMENT = 1, /* bad shape / stride / pointer / flag */
+  CC1D_ERR_UNSUPPORTED = 2,      /* width or dtype outside the supported set */
+  CC1D_ERR_CUDA = 3,             /* a CUDA runtime call or launch failed */
+  CC1D_ERR_WORKSPACE = 4         /* workspace missing or too small */
+};
+
+/*
+ * Forward pass of causal_conv1d_fn.
+ *   out[b,c,t] = act(bias[c] + sum_{k<W} weight[c,k] * xc[b,c,t-(W-1)+k])
+ * where xc is x preceded by initial_states (or by zeros), act is SiLU when
+ * `silu` != 0, and with seq_idx a tap is used only when
+ * seq_idx[b,src] == seq_idx[b,t]; seq_idx[b,t] < 0 forces out = 0.
+ * final_states (optional) receives the last W-1 columns of
+ * cat([initial_states or zeros, x], -1) bit-exactly.
+ *
+ * Replaces the 29-tuple built by `native_fwd`
+ * (src/causal_conv1d_mojo/fwd/__init__.py:27-59) plus the torch copy in
+ * `_write_final_states` (src/causal_conv1d_mojo/_fn.py:31-50).
+ */
+typedef struct cc1d_fwd_params {
+  int32_t dtype;   /* enum cc1d_dtype; x, weight, bias, states and out share it */
+  int32_t width;   /* W: 2..9 for fp16/bf16, 2..5 for fp32 */
+  int64_t batch, dim, seqlen;
+  int32_t silu;    /* 1: SiLU (= swish) activation, 0: none */
+  int32_t _pad0;
+  const void* x;            int64_t x_batch_stride, x_dim_stride, x_seq_stride;
+  const void* weight;       int64_t weight_dim_stride, weight_width_stride;
+  const void* bias;         int64_t bias_stride;          /* NULL: no bias */
+  const int32_t* seq_idx;   int64_t seq_idx_batch_stride, seq_idx_seq_stride; /* NULL: none */
+  const void* initial_states; int64_t init_batch_stride, init_dim_stride, init_seq_stride; /* NULL: zeros */
+  void* out;                int64_t out_batch_stride, out_dim_stride, out_seq_stride;
+  void* final_states;       int64_t final_batch_stride, final_dim_stride, final_seq_stride; /* NULL: not written */
+} cc1d_fwd_params;
+
+CC1D_API int cc1d_fwd(const cc1d_fwd_params* params, void* stream);
+
+/*
+ * Fused backward of causal_conv1d_fn: recomputes the pre-activation and
+ * produces dx, dinitial_states (when initial_states is given), and the fp32
+ * weight/bias gradient sums.  dfinal_states (optional) is folded into dx and
+ * dinitial_states, so no separate tail-add is needed.
+ *
+ * dweight/dbias: the kernel writes per-block partial sums into `workspace`
+ * (size from cc1d_bwd_workspace_size) and a second kernel reduces them in a
+ * fixed order -- results are bitwise reproducible run to run.  The reduced
+ * fp32 sums are OVERWRITTEN (not accumulated) into `dwdb_acc`, a contiguous
+ * fp32 buffer of dim*(W+1) floats laid out as [dweight (dim, W) | dbias (dim)]
+ * so that one all-reduce covers both when the batch is sharded across GPUs.
+ * Optionally the same sums are also written rounded to `dtype` into
+ * `dweight_out` / `dbias_out`.
+ *
+ * Replaces the 39-tuple built by `native_bwd_full`
+ * (src/causal_conv1d_mojo/bwd_full/__init__.py:150-193) and the Python
+ * post-processing in `_CausalConv1dFn.backward`
+ * (src/causal_conv1d_mojo/_fn.py:274-332: dout.contiguous(), zeroed fp32
+ * accumulators, the dfinal_states tail add and the dtype casts).
+ */
+typedef struct cc1d_bwd_params {
+  int32_t dtype;
+  int32_t width;
+  int64_t batch, dim, seqlen;
+  int32_t silu;
+  int32_t _pad0;
+  const void* x;            int64_t x_batch_stride, x_dim_stride, x_seq_stride;
+  const void* weight;       int64_t weight_dim_stride, weight_width_stride;
+  const void* bias;         int64_t bias_stride;          /* NULL: no bias (dbias not produced) */
+  const void* dout;         int64_t dout_batch_stride, dout_dim_stride, dout_seq_stride;
+  const int32_t* seq_idx;   int64_t seq_idx_batch_stride, seq_idx_seq_stride;
+  const void* initial_states; int64_t init_batch_stride, init_dim_stride, init_seq_stride;
+  const void* dfinal_states;  int64_t dfinal_batch_stride, dfinal_dim_stride, dfinal_seq_stride; /* NULL: none */
+  void* dx;                 int64_t dx_batch_stride, dx_dim_stride, dx_seq_stride;
+  void* dinitial_states;    int64_t dinit_batch_stride, dinit_dim_stride, dinit_seq_stride; /* required iff initial_states */
+  float* dwdb_acc;          /* required: dim*(W+1) fp32, contiguous */
+  void* dweight_out;        int64_t dweight_dim_stride, dweight_width_stride; /* NULL: skip */
+  void* dbias_out;          int64_t dbias_stride;        /* NULL: skip */
+  void* workspace;          size_t workspace_bytes;
+} cc1d_bwd_params;
+
+/* Bytes of scratch cc1d_bwd needs for `params` (only shapes, dtype, width and
+ * strides are read).  Writes 0 to *bytes when the call would launch nothing. */
+CC1D_API int cc1d_bwd_workspace_size(const cc1d_bwd_params* params, size_t* bytes);
+
+CC1D_API int cc1d_bwd(const cc1d_bwd_params* params, void* stream);
+
+/*
+ * Decode step of causal_conv1d_update.  x is (batch, dim, seqlen) (a 2-D x of
+ * the Python API is passed with seqlen = 1).  conv_state is
+ * (rows, dim, state_len) with state_len >= W-1, mutated in place:
+ *   linear (cache_seqlens == NULL): shift left by seqlen, append x;
+ *   circular: history read at [cache_seqlens[b]-(W-1), cache_seqlens[b]) and
+ *             x written from cache_seqlens[b], both modulo state_len.
+ * conv_state_indices (optional) redirects batch row b to state row
+ * conv_state_indices[b]; a negative index zeroes out[b] and leaves the state
+ * untouched.  cache_seqlens is always indexed by b.
+ *
+ * Replaces the 29-tuple built by `native_update`
+ * (src/causal_conv1d_mojo/update/__init__.py:27-60).
+ */
+typedef struct cc1d_update_params {
+  int32_t dtype;
+  int32_t width;          /* 2..9 for every dtype */
+  int64_t batch, dim, seqlen, state_len;
+  int64_t state_rows;     /* conv_state.shape[0] (pool size when indexed) */
+  int32_t silu;
+  int32_t _pad0;
+  const void* x;          int64_t x_batch_stride, x_dim_stride, x_seq_stride;
+  const void* weight;     int64_t weight_dim_stride, weight_width_stride;
+  const void* bias;       int64_t bias_stride;
+  void* conv_state;       int64_t state_batch_stride, state_dim_stride, state_seq_stride;
+  const int32_t* conv_state_indices; /* NULL: row b serves batch b */
+  const int32_t* cache_seqlens;      /* NULL: linear mode */
+  void* out;              int64_t out_batch_stride, out_dim_stride, out_seq_stride;
+} cc1d_update_params;
+
+CC1D_API int cc1d_update(const cc1d_update_params* params, void* stream);
+
+/*
+ * causal_conv1d_varlen_states: for each packed sequence i (tokens
+ * [cu_seqlens[i], cu_seqlens[i+1]) of x (total_tokens, dim)), copy its last
+ * state_len tokens into states[i, :, state_len-n:] and zero the rest.
+ * Bit-exact data movement.
+ * Replaces the Python loop of causal_conv1d_varlen_states
+ * (src/causal_conv1d_mojo/causal_conv1d_varlen.py:29-61).
+ */
+typedef struct cc1d_varlen_states_params {
+  int32_t dtype;
+  int32_t _pad0;
+  int64_t batch, dim, state_len, total_tokens;
+  const void* x;              int64_t x_token_stride, x_dim_stride;
+  const int32_t* cu_seqlens;  /* batch+1 entries, non-decreasing */
+  void* states;               int64_t states_batch_stride, states_dim_stride, states_seq_stride;
+} cc1d_varlen_states_params;
+
+CC1D_API int cc1d_varlen_states(const cc1d_varlen_states_params* params, void* stream);
+
+/* Message of the last failed call on this thread ("" if none). */
+CC1D_API const char* cc1d_last_error(void);
+
+/* Version of the Python API this library backs ("1.6.1", as the reference's
+ * __version__, src/causal_conv1d_mojo/__init__.py:51). */
+CC1D_API const char* cc1d_version(void);
+
+/* CC1D_ABI_VERSION of the loaded library. */
+CC1D_API int cc1d_abi_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* CC1D_H_ */

@@ -1,0 +1,122 @@
+"""Production-pattern integration on the GPU: CUDA-graph capture/replay
+(reference tests/test_cuda_graph.py:43-131), torch.compile(fullgraph=True)
+(reference tests/test_fwd.py:494-531), launches on a non-default stream, and
+that the native library -- not some fallback -- is what runs."""
+
+from __future__ import annotations
+
+import pytest
+import torch
+
+from causal_conv1d_b200 import _lib, causal_conv1d_fn, causal_conv1d_update
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda"
+
+
+def test_native_library_is_loaded():
+    import ctypes
+
+    _lib.load()
+    with open("/proc/self/maps") as f:
+        maps = f.read()
+    assert _lib.LIB_NAME in maps
+    assert isinstance(_lib.load(), ctypes.CDLL)
+
+
+def test_cuda_graph_capture_and_replay_matches_eager():
+    B, D, L, W = 2, 64, 128, 4
+    x = torch.randn(B, D, L, dtype=torch.float16, device=DEV)
+    w = torch.randn(D, W, dtype=torch.float16, device=DEV)
+    b = torch.randn(D, dtype=torch.float16, device=DEV)
+    causal_conv1d_fn(x, w, b, activation="silu")  # warm-up outside capture
+    out_buf = torch.empty_like(x)
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        out_buf.copy_(causal_conv1d_fn(x, w, b, activation="silu"))
+    g.replay()
+    torch.cuda.synchronize()
+    assert torch.equal(out_buf, causal_conv1d_fn(x, w, b, activation="silu"))
+    x.add_(0.5)
+    g.replay()
+    torch.cuda.synchronize()
+    assert torch.equal(out_buf, causal_conv1d_fn(x, w, b, activation="silu"))
+
+
+def test_cuda_graph_fwd_bwd_and_update():
+    B, D, L, W = 2, 256, 512, 4
+    x = torch.randn(B, L, D, dtype=torch.bfloat16, device=DEV).transpose(1, 2).requires_grad_()
+    w = torch.randn(D, W, dtype=torch.bfloat16, device=DEV, requires_grad=True)
+    dout = torch.randn(B, L, D, dtype=torch.bfloat16, device=DEV).transpose(1, 2)
+    state = torch.randn(B, D, W - 1, dtype=torch.bfloat16, device=DEV)
+    xt = torch.randn(B, D, dtype=torch.bfloat16, device=DEV)
+
+    def step():
+        out = causal_conv1d_fn(x, w, activation="silu")
+        gx, gw = torch.autograd.grad(out, (x, w), dout)
+        y = causal_conv1d_update(xt, state, w.detach(), activation="silu")
+        return gx, gw, y
+
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        for _ in range(2):
+            step()
+    torch.cuda.current_stream().wait_stream(s)
+    st0 = state.clone()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        gx, gw, y = step()
+    state.copy_(st0)
+    g.replay()
+    torch.cuda.synchronize()
+    state_after = state.clone()
+    state.copy_(st0)
+    ex, ew, ey = step()
+    torch.cuda.synchronize()
+    assert torch.equal(gx, ex) and torch.equal(gw, ew) and torch.equal(y, ey)
+    assert torch.equal(state_after, state)
+
+
+def test_torch_compile_fullgraph():
+    B, D, L = 2, 64, 128
+    x = torch.randn(B, D, L, dtype=torch.float16, device=DEV)
+    w = torch.randn(D, 4, dtype=torch.float16, device=DEV)
+    b = torch.randn(D, dtype=torch.float16, device=DEV)
+
+    @torch.compile(fullgraph=True)
+    def f(x, w, b):
+        return causal_conv1d_fn(x, w, b, activation="silu")
+
+    assert torch.equal(f(x, w, b), causal_conv1d_fn(x, w, b, activation="silu"))
+
+
+def test_torch_compile_autograd():
+    B, D, L = 2, 64, 128
+    x = torch.randn(B, D, L, dtype=torch.float16, device=DEV, requires_grad=True)
+    w = torch.randn(D, 4, dtype=torch.float16, device=DEV, requires_grad=True)
+    b = torch.randn(D, dtype=torch.float16, device=DEV, requires_grad=True)
+
+    @torch.compile
+    def f(x, w, b):
+        return causal_conv1d_fn(x, w, b, activation="silu").sum()
+
+    f(x, w, b).backward()
+    assert x.grad is not None and w.grad is not None and b.grad is not None
+    x2, w2, b2 = (t.detach().clone().requires_grad_() for t in (x, w, b))
+    causal_conv1d_fn(x2, w2, b2, activation="silu").sum().backward()
+    assert torch.equal(x.grad, x2.grad) and torch.equal(w.grad, w2.grad)
+
+
+def test_non_default_stream():
+    B, D, L = 2, 128, 4096
+    x = torch.randn(B, D, L, dtype=torch.bfloat16, device=DEV)
+    w = torch.randn(D, 4, dtype=torch.bfloat16, device=DEV)
+    ref = causal_conv1d_fn(x, w, activation="silu")
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        out = causal_conv1d_fn(x, w, activation="silu")
+    torch.cuda.current_stream().wait_stream(s)
+    torch.cuda.synchronize()
+    assert torch.equal(out, ref)
