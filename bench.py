@@ -77,6 +77,16 @@ class Clocks:
         self.index = index
         self.samples = []
         self.proc = None
+        self.window = [None, None]
+
+    def mark(self):
+        """Start of the timed region (samples before it are dropped)."""
+        time.sleep(0.3)  # let nvidia-smi come up
+        self.window[0] = len(self.samples)
+
+    def unmark(self):
+        time.sleep(0.15)
+        self.window[1] = len(self.samples)
 
     def __enter__(self):
         try:
@@ -105,6 +115,10 @@ class Clocks:
         return False
 
     def summary(self):
+        if self.window[0] is not None:
+            lo = self.window[0]
+            hi = self.window[1] if self.window[1] is not None else len(self.samples)
+            self.samples = self.samples[lo:max(hi, lo + 1)]
         if not self.samples:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
         sm = sorted(float(s[0]) for s in self.samples if s[0].replace(".", "").isdigit())
@@ -176,6 +190,28 @@ def make_c2(seed, device):
     return x, w, b, init, dout
 
 
+def graph_of(fn, n=1):
+    """CUDA graph of `n` calls fn(i) (captured after the caller's warm-up)."""
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        for i in range(n):
+            fn(i)
+    return g
+
+
+def graph_ms(g, reps, per_graph):
+    """Average CUDA-event time of one of the `per_graph` launches in `g`."""
+    g.replay()
+    torch.cuda.synchronize()
+    a, c = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(reps):
+        g.replay()
+    c.record()
+    torch.cuda.synchronize()
+    return a.elapsed_time(c) / (reps * per_graph)
+
+
 def time_c2(args, world, rank):
     from causal_conv1d_b200 import _ops
     from causal_conv1d_b200.parallel import allreduce_weight_grads, split_dwdb
@@ -189,40 +225,52 @@ def time_c2(args, world, rank):
     db = torch.empty(D, dtype=DT, device="cuda")
     dinit = torch.empty_like(init)
     K = args.steps
-    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(K)]
 
-    def step(e=None):
-        if e is not None:
-            e[0].record()
+    def fwd(_=0):
         _ops.fwd(x, w, b, None, init, out, True, fs)
-        if e is not None:
-            e[1].record()
+
+    def bwd(_=0):
         if world > 1:
             _ops.bwd(x, w, b, dout, None, init, None, dx, dwdb, dinit, None, None, True)
-            if e is not None:
-                e[2].record()
+        else:
+            _ops.bwd(x, w, b, dout, None, init, None, dx, dwdb, dinit, dw, db, True)
+
+    def step(_=0):
+        fwd()
+        bwd()
+        if world > 1:
             allreduce_weight_grads(dwdb)
             gw, gb = split_dwdb(dwdb, D, W)
             dw.copy_(gw)
             db.copy_(gb)
-        else:
-            _ops.bwd(x, w, b, dout, None, init, None, dx, dwdb, dinit, dw, db, True)
-            if e is not None:
-                e[2].record()
 
-    for _ in range(args.warmup):
-        step()
-    barrier_sync(world)
-    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with Clocks(torch.cuda.current_device()) as clk:
+        # The sampler starts before the warm-up so that it is already
+        # reporting when the timed steps run.
+        for _ in range(args.warmup):
+            step()
+        torch.cuda.synchronize()
+        # The timed step is replayed from a CUDA graph (captured once), as a
+        # serving / training loop would; every replay launches the same
+        # kernels on the same buffers.
+        g_step = graph_of(step)
+        for _ in range(args.warmup):
+            g_step.replay()
+        barrier_sync(world)
+        clk.mark()
+        start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         start.record()
-        for k in range(K):
-            step(ev[k])
+        for _ in range(K):
+            g_step.replay()
         stop.record()
         torch.cuda.synchronize()
+        clk.unmark()
     total_ms = start.elapsed_time(stop)
-    fwd_ms = sum(e[0].elapsed_time(e[1]) for e in ev) / K
-    bwd_ms = sum(e[1].elapsed_time(e[2]) for e in ev) / K
+    # Per-op kernel times: graphs of the op alone, replayed back to back.
+    reps = max(20, min(200, K // 10))
+    fwd_ms = graph_ms(graph_of(fwd, 10), reps, 10)
+    bwd_ms = graph_ms(graph_of(bwd, 10), reps, 10)
+    del g_step
     barrier_sync(world)
     total_ms = max_over_ranks(total_ms, world)
     return dict(ms_per_step=total_ms / K, fwd_ms=fwd_ms, bwd_ms=bwd_ms, clocks=clk.summary())
@@ -278,17 +326,14 @@ def time_e2e(args, world, rank):
 
 
 def _kernel_ms(fn, iters, sets):
-    """Average CUDA-event time of fn(i) cycling over `sets` buffer sets."""
-    for i in range(3):
-        fn(i % sets)
+    """Average time of fn(i), i cycling over `sets` buffer sets: a CUDA graph
+    of max(sets, 8) launches replayed back to back (no host launch overhead)."""
+    n = max(sets, 8)
+    for i in range(sets):
+        fn(i)
     torch.cuda.synchronize()
-    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(iters)]
-    for i, (a, c) in enumerate(evs):
-        a.record()
-        fn(i % sets)
-        c.record()
-    torch.cuda.synchronize()
-    return sum(a.elapsed_time(c) for a, c in evs) / iters
+    g = graph_of(lambda i: fn(i % sets), n)
+    return graph_ms(g, max(1, iters // n), n)
 
 
 def time_kernels(peak):
@@ -312,7 +357,7 @@ def time_kernels(peak):
     pools = [rn(512, Du, W - 1) for _ in range(sets)]
     idx = [torch.randperm(512, device="cuda")[:Bu].to(torch.int32) for _ in range(sets)]
     outs = [torch.empty_like(xs[0]) for _ in range(sets)]
-    ms = _kernel_ms(lambda i: _ops.update(xs[i], pools[i], w, b, None, idx[i], outs[i], True), 50, sets)
+    ms = _kernel_ms(lambda i: _ops.update(xs[i], pools[i], w, b, None, idx[i], outs[i], True), 800, sets)
     nbytes = Bu * Du * (2 + 2 + 6 + 6) + Du * (W + 1) * 2 + Bu * 4
     res["update_c3a_indexed"] = dict(ms=ms, gbs=nbytes / ms / 1e6, frac=nbytes / ms / 1e6 / peak,
                                      tokens_per_s=Bu / (ms / 1e3), algorithmic_bytes=nbytes)
@@ -320,7 +365,7 @@ def time_kernels(peak):
     # C3b: circular (256, 5376, 8), cache_seqlens ~ U{0..1023}.
     states = [rn(Bu, Du, 8) for _ in range(sets)]
     cache = [torch.randint(0, 1024, (Bu,), device="cuda", dtype=torch.int32) for _ in range(sets)]
-    ms = _kernel_ms(lambda i: _ops.update(xs[i], states[i], w, b, cache[i], None, outs[i], True), 50, sets)
+    ms = _kernel_ms(lambda i: _ops.update(xs[i], states[i], w, b, cache[i], None, outs[i], True), 800, sets)
     nbytes = Bu * Du * (2 + 2 + 6 + 2) + Du * (W + 1) * 2 + Bu * 4
     res["update_c3b_circular"] = dict(ms=ms, gbs=nbytes / ms / 1e6, frac=nbytes / ms / 1e6 / peak,
                                       tokens_per_s=Bu / (ms / 1e3), algorithmic_bytes=nbytes)
@@ -466,7 +511,7 @@ def load_traffic():
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--steps", type=int, default=2000)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--skip-kernels", action="store_true", help="skip the secondary kernel table")

@@ -103,6 +103,7 @@ SIGNATURES = {
     "cc1d_bwd": (c_i32, [ctypes.POINTER(BwdParams), c_ptr]),
     "cc1d_update": (c_i32, [ctypes.POINTER(UpdateParams), c_ptr]),
     "cc1d_varlen_states": (c_i32, [ctypes.POINTER(VarlenParams), c_ptr]),
+    "cc1d_device_status": (c_i32, [ctypes.POINTER(ctypes.c_uint)]),
     "cc1d_last_error": (ctypes.c_char_p, []),
     "cc1d_version": (ctypes.c_char_p, []),
     "cc1d_abi_version": (c_i32, []),
@@ -146,3 +147,12 @@ def check(status: int, what: str) -> None:
     if status != CC1D_OK:
         msg = load().cc1d_last_error().decode(errors="replace")
         raise Cc1dError(status, f"{what} failed (status {status}): {msg}")
+
+
+def device_wait_timeouts() -> int:
+    """Bounded in-kernel waits that gave up since the last call (and reset
+    the count); synchronises the current device."""
+    lib = load()
+    n = ctypes.c_uint(0)
+    check(lib.cc1d_device_status(ctypes.byref(n)), "cc1d_device_status")
+    return int(n.value)

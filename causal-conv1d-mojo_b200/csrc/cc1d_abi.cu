@@ -155,9 +155,10 @@ int cc1d_fwd(const cc1d_fwd_params* p, void* stream) {
   }
   Plan plan;
   std::memset(&plan, 0, sizeof(plan));
-  cudaError_t e = plan_fwd(p->dtype, p->width, a, &plan);
+  const bool tma = fwd_tma_eligible(p->dtype, a);
+  cudaError_t e = tma ? plan_fwd_tma(p->dtype, p->width, a, &plan) : plan_fwd(p->dtype, p->width, a, &plan);
   if (e != cudaSuccess) return cuda_fail(e, "cc1d_fwd plan");
-  e = launch_fwd(p->dtype, p->width, a, plan, s);
+  e = tma ? launch_fwd_tma(p->dtype, p->width, a, plan, s) : launch_fwd(p->dtype, p->width, a, plan, s);
   if (e != cudaSuccess) return cuda_fail(e, "cc1d_fwd launch");
   return ok();
 }
@@ -171,7 +172,8 @@ int cc1d_bwd_workspace_size(const cc1d_bwd_params* p, size_t* bytes) {
   if (p->batch * p->dim * p->seqlen == 0) return ok();
   Plan plan;
   std::memset(&plan, 0, sizeof(plan));
-  cudaError_t e = plan_bwd(p->dtype, p->width, a, &plan);
+  cudaError_t e = bwd_tma_eligible(p->dtype, a) ? plan_bwd_tma(p->dtype, p->width, a, &plan)
+                                                 : plan_bwd(p->dtype, p->width, a, &plan);
   if (e != cudaSuccess) return cuda_fail(e, "cc1d_bwd plan");
   *bytes = partial_bytes(plan, p->dim, p->width);
   return ok();
@@ -187,13 +189,14 @@ int cc1d_bwd(const cc1d_bwd_params* p, void* stream) {
   std::memset(&plan, 0, sizeof(plan));
   cudaError_t e = cudaSuccess;
   if (p->batch * p->seqlen > 0) {
-    e = plan_bwd(p->dtype, p->width, a, &plan);
+    const bool tma = bwd_tma_eligible(p->dtype, a);
+    e = tma ? plan_bwd_tma(p->dtype, p->width, a, &plan) : plan_bwd(p->dtype, p->width, a, &plan);
     if (e != cudaSuccess) return cuda_fail(e, "cc1d_bwd plan");
     const size_t need = partial_bytes(plan, p->dim, p->width);
     if (need > 0 && (p->workspace == nullptr || p->workspace_bytes < need))
       return fail(CC1D_ERR_WORKSPACE, "cc1d_bwd: workspace of %zu bytes needed, %zu given", need,
                   p->workspace == nullptr ? (size_t)0 : p->workspace_bytes);
-    e = launch_bwd(p->dtype, p->width, a, plan, s);
+    e = tma ? launch_bwd_tma(p->dtype, p->width, a, plan, s) : launch_bwd(p->dtype, p->width, a, plan, s);
     if (e != cudaSuccess) return cuda_fail(e, "cc1d_bwd launch");
   } else if (p->batch > 0 && p->seqlen == 0) {
     e = launch_bwd_empty_seq(p->dtype, p->width, a, s);
@@ -250,6 +253,13 @@ int cc1d_varlen_states(const cc1d_varlen_states_params* p, void* stream) {
                p->batch, p->dim, p->state_len, p->total_tokens};
   cudaError_t e = launch_varlen_states(p->dtype, a, static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_fail(e, "cc1d_varlen_states launch");
+  return ok();
+}
+
+int cc1d_device_status(unsigned* wait_timeouts) {
+  if (wait_timeouts == nullptr) return fail(CC1D_ERR_INVALID_ARGUMENT, "cc1d_device_status: NULL output");
+  cudaError_t e = read_wait_timeouts(wait_timeouts);
+  if (e != cudaSuccess) return cuda_fail(e, "cc1d_device_status");
   return ok();
 }
 

@@ -101,15 +101,84 @@ __device__ __forceinline__ void store_strided(T* __restrict__ p, i64 stride, int
   }
 }
 
-// SiLU(v) = v * sigmoid(v), evaluated with the fast exp and divide
-// intrinsics (the op is SFU-bound otherwise).
-__device__ __forceinline__ float silu_f(float v) { return __fdividef(v, 1.0f + __expf(-v)); }
+// SiLU(v) = v * sigmoid(v), sigmoid(v) = 1 / (1 + exp(-v)) with
+// exp(-v) = 2^(-v * log2(e)), each step one hardware instruction: the
+// approximate base-2 exponential (ex2.approx, rel. error ~2^-22) and the
+// approximate reciprocal (rcp.approx, ~1 ulp).  At v << 0, 2^(...) = inf and
+// the reciprocal is 0, so SiLU -> -0 and SiLU' -> 0.  Every kernel (scalar or
+// packed) evaluates exactly this sequence, so the forward, the decode update
+// and the backward recomputation agree bit for bit.
+constexpr float kNegLog2e = -1.4426950408889634f;
+
+__device__ __forceinline__ float ex2_approx(float v) {
+  float r;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(v));
+  return r;
+}
+
+__device__ __forceinline__ float rcp_approx(float v) {
+  float r;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(v));
+  return r;
+}
+
+__device__ __forceinline__ float sigmoid_f(float v) { return rcp_approx(1.0f + ex2_approx(v * kNegLog2e)); }
+__device__ __forceinline__ float silu_f(float v) { return v * sigmoid_f(v); }
 
 // d SiLU / dv = s * (1 + v * (1 - s)) with s = sigmoid(v).
 __device__ __forceinline__ float silu_grad_f(float v) {
-  const float s = __fdividef(1.0f, 1.0f + __expf(-v));
-  return s * (1.0f + v * (1.0f - s));
+  const float s = sigmoid_f(v);
+  return s * fmaf(v, fmaf(s, -1.0f, 1.0f), 1.0f);
 }
+
+// ---- two adjacent channels per thread, packed fp32 math (sm_100 FFMA2) ----
+
+__device__ __forceinline__ float2 f2(float a, float b) { return make_float2(a, b); }
+__device__ __forceinline__ float2 fma2(float2 a, float2 b, float2 c) { return __ffma2_rn(a, b, c); }
+__device__ __forceinline__ float2 add2(float2 a, float2 b) { return __fadd2_rn(a, b); }
+__device__ __forceinline__ float2 mul2(float2 a, float2 b) { return __fmul2_rn(a, b); }
+
+__device__ __forceinline__ float2 sigmoid2(float2 v) {
+  const float2 t = mul2(v, f2(kNegLog2e, kNegLog2e));
+  const float2 d = add2(f2(1.0f, 1.0f), f2(ex2_approx(t.x), ex2_approx(t.y)));
+  return f2(rcp_approx(d.x), rcp_approx(d.y));
+}
+__device__ __forceinline__ float2 silu2(float2 v) { return mul2(v, sigmoid2(v)); }
+__device__ __forceinline__ float2 silu_grad2(float2 v) {
+  const float2 s = sigmoid2(v);
+  const float2 one = f2(1.0f, 1.0f);
+  return mul2(s, fma2(v, fma2(s, f2(-1.0f, -1.0f), one), one));
+}
+
+// Storage word of two adjacent elements and its conversion to/from float2.
+template <typename T>
+struct Pair;
+template <>
+struct Pair<__nv_bfloat16> {
+  typedef uint32_t W;
+  static __device__ __forceinline__ float2 unpack(W w) {
+    return f2(__uint_as_float(w << 16), __uint_as_float(w & 0xffff0000u));
+  }
+  static __device__ __forceinline__ W pack(float2 v) {
+    __nv_bfloat162 h = __float22bfloat162_rn(v);
+    return *reinterpret_cast<W*>(&h);
+  }
+};
+template <>
+struct Pair<__half> {
+  typedef uint32_t W;
+  static __device__ __forceinline__ float2 unpack(W w) { return __half22float2(*reinterpret_cast<__half2*>(&w)); }
+  static __device__ __forceinline__ W pack(float2 v) {
+    __half2 h = __float22half2_rn(v);
+    return *reinterpret_cast<W*>(&h);
+  }
+};
+template <>
+struct Pair<float> {
+  typedef float2 W;
+  static __device__ __forceinline__ float2 unpack(W w) { return w; }
+  static __device__ __forceinline__ W pack(float2 v) { return v; }
+};
 
 __host__ __device__ __forceinline__ i64 ceil_div(i64 a, i64 b) { return (a + b - 1) / b; }
 

@@ -113,6 +113,18 @@ cudaError_t launch_bwd_empty_seq(int dtype, int width, const BwdArgs& a, cudaStr
 // Length-0 sequences: final_states = initial_states (or 0).
 cudaError_t launch_fwd_empty_seq(int dtype, int width, const FwdArgs& a, cudaStream_t stream);
 
+// TMA-pipelined channel-last kernels (cc1d_chan_tma.cu); used when the
+// strides and alignment allow tensor-map tile loads.
+bool fwd_tma_eligible(int dtype, const FwdArgs& a);
+cudaError_t plan_fwd_tma(int dtype, int width, const FwdArgs& a, Plan* plan);
+cudaError_t launch_fwd_tma(int dtype, int width, const FwdArgs& a, const Plan& plan, cudaStream_t stream);
+bool bwd_tma_eligible(int dtype, const BwdArgs& a);
+cudaError_t plan_bwd_tma(int dtype, int width, const BwdArgs& a, Plan* plan);
+cudaError_t launch_bwd_tma(int dtype, int width, const BwdArgs& a, const Plan& plan, cudaStream_t stream);
+
+// Reads and clears the device-side count of bounded waits that gave up.
+cudaError_t read_wait_timeouts(unsigned* count);
+
 cudaError_t launch_update(int dtype, int width, const UpdateArgs& a, cudaStream_t stream);
 cudaError_t launch_varlen_states(int dtype, const VarlenArgs& a, cudaStream_t stream);
 

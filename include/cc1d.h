@@ -177,6 +177,13 @@ typedef struct cc1d_varlen_states_params {
 
 CC1D_API int cc1d_varlen_states(const cc1d_varlen_states_params* params, void* stream);
 
+/* Diagnostics: *wait_timeouts receives the number of bounded in-kernel waits
+ * (pipeline barriers) that gave up since the previous call, on the current
+ * device, and the count is reset.  A non-zero count means some results of
+ * the kernels launched meanwhile are invalid.  Synchronises the device.
+ * No reference counterpart (the reference kernels have no in-kernel waits). */
+CC1D_API int cc1d_device_status(unsigned* wait_timeouts);
+
 /* Message of the last failed call on this thread ("" if none). */
 CC1D_API const char* cc1d_last_error(void);
 

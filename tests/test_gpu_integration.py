@@ -120,3 +120,16 @@ def test_non_default_stream():
     torch.cuda.current_stream().wait_stream(s)
     torch.cuda.synchronize()
     assert torch.equal(out, ref)
+
+
+def test_pipeline_waits_never_time_out():
+    """The TMA pipelines' bounded mbarrier waits all completed (the device
+    counter of given-up waits stays 0) across the layouts that use them."""
+    _lib.device_wait_timeouts()  # clear
+    for D, L in [(256, 1000), (5376, 777), (264, 31)]:
+        x = torch.randn(3, L, D, dtype=torch.bfloat16, device=DEV).transpose(1, 2).requires_grad_()
+        w = torch.randn(D, 4, dtype=torch.bfloat16, device=DEV, requires_grad=True)
+        init = torch.randn(3, D, 3, dtype=torch.bfloat16, device=DEV, requires_grad=True)
+        out, fs = causal_conv1d_fn(x, w, initial_states=init, return_final_states=True, activation="silu")
+        torch.autograd.backward([out, fs], [torch.randn_like(out), torch.randn_like(fs)])
+    assert _lib.device_wait_timeouts() == 0
