@@ -31,8 +31,9 @@ namespace cc1d {
 
 namespace {
 
-// Pipeline shape.  Defaults chosen by measurement on B200 (see DESIGN);
-// overridable with -D for tuning sweeps.
+// Pipeline shape.  The defaults were the fastest of a sweep of stage sizes,
+// stage counts and occupancy bounds measured on B200 at the Mamba-2 prefill
+// shape; overridable with -D for tuning sweeps.
 #ifndef CC1D_FWD_STAGE_BYTES
 #define CC1D_FWD_STAGE_BYTES 8192
 #endif

@@ -1,9 +1,9 @@
 """Generates the golden fixtures in this directory from the REFERENCE itself.
 
-Run in a container where the reference checkout is mounted (default
-/root/reference, override with CC1D_REFERENCE):
+Run where a checkout of the reference is available, passing its root:
 
-    python tests/golden/make_golden.py
+    python tests/golden/make_golden.py <reference-checkout>
+    (or set CC1D_REFERENCE=<reference-checkout>)
 
 It imports the reference's pure-PyTorch implementation
 (src/causal_conv1d_mojo/reference.py: causal_conv1d_ref,
@@ -33,7 +33,7 @@ import numpy as np
 import torch
 
 HERE = Path(__file__).resolve().parent
-REF_ROOT = Path(os.environ.get("CC1D_REFERENCE", "/root/reference"))
+REF_ROOT = Path(sys.argv[1] if len(sys.argv) > 1 else os.environ.get("CC1D_REFERENCE", "reference"))
 REF_PY = REF_ROOT / "src" / "causal_conv1d_mojo" / "reference.py"
 
 DT = {"fp32": torch.float32, "bf16": torch.bfloat16, "fp16": torch.float16}
