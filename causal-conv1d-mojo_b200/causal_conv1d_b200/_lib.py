@@ -101,6 +101,7 @@ SIGNATURES = {
     "cc1d_fwd": (c_i32, [ctypes.POINTER(FwdParams), c_ptr]),
     "cc1d_bwd_workspace_size": (c_i32, [ctypes.POINTER(BwdParams), ctypes.POINTER(ctypes.c_size_t)]),
     "cc1d_bwd": (c_i32, [ctypes.POINTER(BwdParams), c_ptr]),
+    "cc1d_bwd_noalloc": (c_i32, [ctypes.POINTER(BwdParams), c_ptr]),
     "cc1d_update": (c_i32, [ctypes.POINTER(UpdateParams), c_ptr]),
     "cc1d_varlen_states": (c_i32, [ctypes.POINTER(VarlenParams), c_ptr]),
     "cc1d_device_status": (c_i32, [ctypes.POINTER(ctypes.c_uint)]),

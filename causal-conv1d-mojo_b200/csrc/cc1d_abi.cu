@@ -49,6 +49,16 @@ std::atomic<int> g_threads_per_sm[kMaxDevices];
 
 }  // namespace
 
+int report_error(int code, const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_err, sizeof(g_err), fmt, ap);
+  va_end(ap);
+  return code;
+}
+
+int report_cuda_error(cudaError_t e, const char* what) { return cuda_fail(e, what); }
+
 cudaError_t device_info(DeviceInfo* out) {
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);

@@ -122,6 +122,11 @@ bool bwd_tma_eligible(int dtype, const BwdArgs& a);
 cudaError_t plan_bwd_tma(int dtype, int width, const BwdArgs& a, Plan* plan);
 cudaError_t launch_bwd_tma(int dtype, int width, const BwdArgs& a, const Plan& plan, cudaStream_t stream);
 
+// Records a message for cc1d_last_error() and returns `code` (for entry
+// points defined outside cc1d_abi.cu).
+int report_error(int code, const char* fmt, ...);
+int report_cuda_error(cudaError_t e, const char* what);
+
 // Reads and clears the device-side count of bounded waits that gave up.
 cudaError_t read_wait_timeouts(unsigned* count);
 

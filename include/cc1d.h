@@ -127,6 +127,24 @@ CC1D_API int cc1d_bwd_workspace_size(const cc1d_bwd_params* params, size_t* byte
 CC1D_API int cc1d_bwd(const cc1d_bwd_params* params, void* stream);
 
 /*
+ * cc1d_bwd for callers that cannot allocate device memory (a serving engine
+ * that reserved almost all of HBM up front, an FFI caller without access to
+ * the host framework's allocator, a loop that must not take cudaMalloc's
+ * implicit synchronisation).  Identical to cc1d_bwd except that
+ * params->workspace / workspace_bytes are ignored: the scratch is a static
+ * device array of CC1D_NOALLOC_SCRATCH_BYTES built into the library, which
+ * every GPU that loads the library holds until the process exits.  Calls
+ * needing more scratch than that (see cc1d_bwd_workspace_size) fail with
+ * CC1D_ERR_WORKSPACE.  The first call on a device looks up the array's
+ * device address (make it before any stream capture).  All calls share the
+ * array: calls that overlap on the GPU race.  No allocation is made.
+ * No counterpart in the reference (its backward allocates through torch).
+ */
+#define CC1D_NOALLOC_SCRATCH_BYTES (16u * 1024u * 1024u)
+
+CC1D_API int cc1d_bwd_noalloc(const cc1d_bwd_params* params, void* stream);
+
+/*
  * Decode step of causal_conv1d_update.  x is (batch, dim, seqlen) (a 2-D x of
  * the Python API is passed with seqlen = 1).  conv_state is
  * (rows, dim, state_len) with state_len >= W-1, mutated in place:
