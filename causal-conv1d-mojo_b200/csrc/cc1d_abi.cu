@@ -142,6 +142,19 @@ int bwd_args(const cc1d_bwd_params* p, BwdArgs* a) {
   return CC1D_OK;
 }
 
+// Backward kernel family: 2 = TMA along seqlen, 1 = TMA along dim, 0 =
+// register streaming.  The workspace size depends on it, so the size query
+// and the launch must agree (both go through here).
+int bwd_family(int dtype, const BwdArgs& a) {
+  return bwd_seq_tma_eligible(dtype, a) ? 2 : (bwd_tma_eligible(dtype, a) ? 1 : 0);
+}
+
+cudaError_t plan_bwd_any(int dtype, int width, const BwdArgs& a, Plan* plan) {
+  const int fam = bwd_family(dtype, a);
+  return fam == 2 ? plan_bwd_seq_tma(dtype, width, a, plan)
+                  : fam == 1 ? plan_bwd_tma(dtype, width, a, plan) : plan_bwd(dtype, width, a, plan);
+}
+
 size_t partial_bytes(const Plan& plan, int64_t dim, int width) {
   return (size_t)plan.n_partials * (size_t)dim * (size_t)(width + 1) * sizeof(float);
 }
@@ -165,10 +178,16 @@ int cc1d_fwd(const cc1d_fwd_params* p, void* stream) {
   }
   Plan plan;
   std::memset(&plan, 0, sizeof(plan));
-  const bool tma = fwd_tma_eligible(p->dtype, a);
-  cudaError_t e = tma ? plan_fwd_tma(p->dtype, p->width, a, &plan) : plan_fwd(p->dtype, p->width, a, &plan);
+  // Kernel family: TMA pipeline along seqlen, TMA pipeline along dim
+  // (channel-last), else register streaming (any strides).
+  const int fam = fwd_seq_tma_eligible(p->dtype, a) ? 2 : (fwd_tma_eligible(p->dtype, a) ? 1 : 0);
+  cudaError_t e = fam == 2   ? plan_fwd_seq_tma(p->dtype, p->width, a, &plan)
+                  : fam == 1 ? plan_fwd_tma(p->dtype, p->width, a, &plan)
+                             : plan_fwd(p->dtype, p->width, a, &plan);
   if (e != cudaSuccess) return cuda_fail(e, "cc1d_fwd plan");
-  e = tma ? launch_fwd_tma(p->dtype, p->width, a, plan, s) : launch_fwd(p->dtype, p->width, a, plan, s);
+  e = fam == 2   ? launch_fwd_seq_tma(p->dtype, p->width, a, plan, s)
+      : fam == 1 ? launch_fwd_tma(p->dtype, p->width, a, plan, s)
+                 : launch_fwd(p->dtype, p->width, a, plan, s);
   if (e != cudaSuccess) return cuda_fail(e, "cc1d_fwd launch");
   return ok();
 }
@@ -182,8 +201,7 @@ int cc1d_bwd_workspace_size(const cc1d_bwd_params* p, size_t* bytes) {
   if (p->batch * p->dim * p->seqlen == 0) return ok();
   Plan plan;
   std::memset(&plan, 0, sizeof(plan));
-  cudaError_t e = bwd_tma_eligible(p->dtype, a) ? plan_bwd_tma(p->dtype, p->width, a, &plan)
-                                                 : plan_bwd(p->dtype, p->width, a, &plan);
+  cudaError_t e = plan_bwd_any(p->dtype, p->width, a, &plan);
   if (e != cudaSuccess) return cuda_fail(e, "cc1d_bwd plan");
   *bytes = partial_bytes(plan, p->dim, p->width);
   return ok();
@@ -199,14 +217,16 @@ int cc1d_bwd(const cc1d_bwd_params* p, void* stream) {
   std::memset(&plan, 0, sizeof(plan));
   cudaError_t e = cudaSuccess;
   if (p->batch * p->seqlen > 0) {
-    const bool tma = bwd_tma_eligible(p->dtype, a);
-    e = tma ? plan_bwd_tma(p->dtype, p->width, a, &plan) : plan_bwd(p->dtype, p->width, a, &plan);
+    const int fam = bwd_family(p->dtype, a);
+    e = plan_bwd_any(p->dtype, p->width, a, &plan);
     if (e != cudaSuccess) return cuda_fail(e, "cc1d_bwd plan");
     const size_t need = partial_bytes(plan, p->dim, p->width);
     if (need > 0 && (p->workspace == nullptr || p->workspace_bytes < need))
       return fail(CC1D_ERR_WORKSPACE, "cc1d_bwd: workspace of %zu bytes needed, %zu given", need,
                   p->workspace == nullptr ? (size_t)0 : p->workspace_bytes);
-    e = tma ? launch_bwd_tma(p->dtype, p->width, a, plan, s) : launch_bwd(p->dtype, p->width, a, plan, s);
+    e = fam == 2   ? launch_bwd_seq_tma(p->dtype, p->width, a, plan, s)
+        : fam == 1 ? launch_bwd_tma(p->dtype, p->width, a, plan, s)
+                   : launch_bwd(p->dtype, p->width, a, plan, s);
     if (e != cudaSuccess) return cuda_fail(e, "cc1d_bwd launch");
   } else if (p->batch > 0 && p->seqlen == 0) {
     e = launch_bwd_empty_seq(p->dtype, p->width, a, s);

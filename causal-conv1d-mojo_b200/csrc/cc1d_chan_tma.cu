@@ -641,7 +641,9 @@ struct BwdTmaOp {
 
 cudaError_t read_wait_timeouts(unsigned* count) {
   *count = 0;
-  return tu_read_wait_timeouts(count);
+  cudaError_t e = tu_read_wait_timeouts(count);
+  if (e != cudaSuccess) return e;
+  return read_seq_wait_timeouts(count);
 }
 
 bool fwd_tma_eligible(int dtype, const FwdArgs& a) {

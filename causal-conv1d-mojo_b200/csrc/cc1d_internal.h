@@ -122,6 +122,15 @@ bool bwd_tma_eligible(int dtype, const BwdArgs& a);
 cudaError_t plan_bwd_tma(int dtype, int width, const BwdArgs& a, Plan* plan);
 cudaError_t launch_bwd_tma(int dtype, int width, const BwdArgs& a, const Plan& plan, cudaStream_t stream);
 
+// TMA-pipelined seqlen-contiguous kernels (cc1d_seq_tma.cu).
+bool fwd_seq_tma_eligible(int dtype, const FwdArgs& a);
+cudaError_t plan_fwd_seq_tma(int dtype, int width, const FwdArgs& a, Plan* plan);
+cudaError_t launch_fwd_seq_tma(int dtype, int width, const FwdArgs& a, const Plan& plan, cudaStream_t stream);
+bool bwd_seq_tma_eligible(int dtype, const BwdArgs& a);
+cudaError_t plan_bwd_seq_tma(int dtype, int width, const BwdArgs& a, Plan* plan);
+cudaError_t launch_bwd_seq_tma(int dtype, int width, const BwdArgs& a, const Plan& plan, cudaStream_t stream);
+cudaError_t read_seq_wait_timeouts(unsigned* count);
+
 // Records a message for cc1d_last_error() and returns `code` (for entry
 // points defined outside cc1d_abi.cu).
 int report_error(int code, const char* fmt, ...);

@@ -1,0 +1,676 @@
+// seqlen-contiguous (x.stride(2) == 1) forward and backward kernels, fed by a
+// TMA pipeline.  sm_100a.
+//
+// Block = 4 consumer warps + 1 producer warp, owning a group of 8 channels of
+// one batch row and a segment of positions.  The producer's elected lane
+// streams [8 channel-rows x 256 positions] tiles (cp.async.bulk.tensor.3d over
+// the (L, D, B) view) into a shared-memory ring guarded by full/empty
+// mbarriers (bounded waits).  Consumer warp w owns channel rows 2w and 2w+1:
+// lane i holds positions [8i, 8i+8) of both rows, packed as (row 2w, row 2w+1)
+// float2 pairs so the conv taps run as sm_100 FFMA2; the W-1 halo of lane i
+// comes from lane i-1 by shuffle, and lane 0 of the next tile takes it from
+// lane 31 of the current one, so x is read from HBM exactly once.
+//
+// The backward walks the tiles forward too.  dx at a position needs dpre of
+// the next W-1 positions; for lane 31 those live in the next tile, so every
+// tile's dx is emitted one tile late (its dpre kept in registers), with the
+// dpre just past the segment computed from a few scalar loads.
+// Semantics are those of cc1d_fwd.cu / cc1d_bwd.cu (reference CPU kernels
+// src/causal_conv1d_mojo/fwd_cpu/kernel.mojo:64-117,
+// bwd_full_cpu/kernel.mojo:26-314; final/initial states as
+// src/causal_conv1d_mojo/reference.py:50-56).  seq_idx calls use the
+// register-streaming kernels.
+#include <cudaTypedefs.h>
+
+#include <type_traits>
+
+#include "cc1d_dispatch.cuh"
+#include "cc1d_tma.cuh"
+
+namespace cc1d {
+
+namespace {
+
+constexpr int kSW = 4;              // consumer warps
+constexpr int kRows = 2 * kSW;      // channel rows per tile
+constexpr int kTL = 256;            // positions per tile (32 lanes x 8)
+constexpr int kThreadsSeq = (kSW + 1) * 32;
+
+template <typename T>
+constexpr unsigned seq_tile_bytes() {
+  return kTL * kRows * sizeof(T);
+}
+template <typename T>
+constexpr int seq_fwd_stages() {
+  return 32768 / seq_tile_bytes<T>();  // 16-bit: 8, fp32: 4
+}
+template <typename T>
+constexpr int seq_bwd_stages() {
+  return 49152 / (2 * seq_tile_bytes<T>());  // 16-bit: 6, fp32: 3
+}
+
+struct alignas(64) SeqFwdParams {
+  CUtensorMap map_x;
+  FwdArgs a;
+  i64 groups;
+};
+struct alignas(64) SeqBwdParams {
+  CUtensorMap map_x;
+  CUtensorMap map_g;
+  BwdArgs a;
+  i64 groups;
+};
+
+// The 8 positions [8*lane, 8*lane+8) of tile row r, converted to float.
+template <typename T>
+__device__ __forceinline__ void lds8(const unsigned char* tile, int r, int lane, float (&v)[8]) {
+  const T* p = reinterpret_cast<const T*>(tile) + r * kTL + lane * 8;
+  if constexpr (sizeof(T) == 2) {
+    const uint4 u = *reinterpret_cast<const uint4*>(p);
+    const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float2 f = Pair<T>::unpack(w[i]);
+      v[2 * i] = f.x;
+      v[2 * i + 1] = f.y;
+    }
+  } else {
+    const float4 a = reinterpret_cast<const float4*>(p)[0];
+    const float4 b = reinterpret_cast<const float4*>(p)[1];
+    v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
+    v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+  }
+}
+
+// Stores 8 consecutive elements (16-byte aligned for 16-bit types).
+template <typename T>
+__device__ __forceinline__ void stg8(T* p, const float (&v)[8]) {
+  if constexpr (sizeof(T) == 2) {
+    uint4 u;
+    u.x = Pair<T>::pack(f2(v[0], v[1]));
+    u.y = Pair<T>::pack(f2(v[2], v[3]));
+    u.z = Pair<T>::pack(f2(v[4], v[5]));
+    u.w = Pair<T>::pack(f2(v[6], v[7]));
+    *reinterpret_cast<uint4*>(p) = u;
+  } else {
+    reinterpret_cast<float4*>(p)[0] = make_float4(v[0], v[1], v[2], v[3]);
+    reinterpret_cast<float4*>(p)[1] = make_float4(v[4], v[5], v[6], v[7]);
+  }
+}
+
+__device__ __forceinline__ float2 shfl_up2(float2 v, int d) {
+  return f2(__shfl_up_sync(kFull, v.x, d), __shfl_up_sync(kFull, v.y, d));
+}
+__device__ __forceinline__ float2 shfl_down2(float2 v, int d) {
+  return f2(__shfl_down_sync(kFull, v.x, d), __shfl_down_sync(kFull, v.y, d));
+}
+__device__ __forceinline__ float2 shfl2(float2 v, int src) {
+  return f2(__shfl_sync(kFull, v.x, src), __shfl_sync(kFull, v.y, src));
+}
+
+// xc (x preceded by initial_states or zeros) at position q of rows (ra, rb).
+template <typename T>
+__device__ __forceinline__ float2 xc_pair(const T* x, i64 xs_c, i64 xs_l, const T* init, i64 is_c, i64 is_l,
+                                          int H, i64 q, bool va, bool vb) {
+  float2 r = f2(0.f, 0.f);
+  if (q >= 0) {
+    if (va) r.x = Cvt<T>::f(x[q * xs_l]);
+    if (vb) r.y = Cvt<T>::f(x[xs_c + q * xs_l]);
+  } else if (init != nullptr) {
+    if (va) r.x = Cvt<T>::f(init[(q + H) * is_l]);
+    if (vb) r.y = Cvt<T>::f(init[is_c + (q + H) * is_l]);
+  }
+  return r;
+}
+
+// ---------------------------------------------------------------------------
+// Forward
+// ---------------------------------------------------------------------------
+
+template <typename T, int W, bool SILU>
+__global__ void __launch_bounds__(kThreadsSeq) fwd_seq_tma_kernel(const __grid_constant__ SeqFwdParams p) {
+  constexpr int H = W - 1;
+  constexpr unsigned TB = seq_tile_bytes<T>();
+  constexpr int NS = seq_fwd_stages<T>();
+  extern __shared__ __align__(128) unsigned char smem[];
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + NS * TB);
+  uint64_t* empty = full + NS;
+  const FwdArgs& a = p.a;
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const i64 item = blockIdx.x;
+  const i64 seg = item % a.nseg;
+  const i64 rest = item / a.nseg;
+  const i64 grp = rest % p.groups;
+  const i64 b = rest / p.groups;
+  const i64 c0 = grp * kRows;
+  const i64 t0 = seg * a.seg_len;
+  const i64 t1 = min(a.L, t0 + a.seg_len);
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < NS; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], kSW);
+    }
+    fence_mbar_init();
+  }
+  __syncthreads();
+
+  if (warp == kSW) {
+    if (lane == 0) {
+      prefetch_tensormap(&p.map_x);
+      unsigned k = 0;
+      for (i64 t = t0; t < t1; t += kTL, ++k) {
+        const unsigned s = k % NS, use = k / NS;
+        if (use > 0 && !mbar_wait(&empty[s], (use - 1) & 1)) return;
+        mbar_arrive_expect_tx(&full[s], TB);
+        tma_load_3d(smem + s * TB, &p.map_x, &full[s], (int)t, (int)c0, (int)b);
+      }
+    }
+    return;
+  }
+
+  const i64 ra = c0 + 2 * warp;  // rows (channels) of this warp: ra, ra + 1
+  const bool va = ra < a.D, vb = ra + 1 < a.D;
+  const T* __restrict__ wt = static_cast<const T*>(a.w);
+  const T* __restrict__ bias = static_cast<const T*>(a.bias);
+  float2 wp[W];
+#pragma unroll
+  for (int k = 0; k < W; ++k)
+    wp[k] = f2(va ? Cvt<T>::f(wt[ra * a.ws_c + k * a.ws_k]) : 0.f, vb ? Cvt<T>::f(wt[(ra + 1) * a.ws_c + k * a.ws_k]) : 0.f);
+  const float2 bp = f2((bias && va) ? Cvt<T>::f(bias[ra * a.bs]) : 0.f, (bias && vb) ? Cvt<T>::f(bias[(ra + 1) * a.bs]) : 0.f);
+  const T* __restrict__ xr = static_cast<const T*>(a.x) + b * a.xs_b + ra * a.xs_c;
+  const T* __restrict__ ir = a.init ? static_cast<const T*>(a.init) + b * a.is_b + ra * a.is_c : nullptr;
+  T* __restrict__ oa = static_cast<T*>(a.out) + b * a.os_b + ra * a.os_c;
+
+  // Halo of lane 0 in the first tile: xc at t0-H .. t0-1.
+  float2 carry[H];
+#pragma unroll
+  for (int j = 0; j < H; ++j) carry[j] = xc_pair(xr, a.xs_c, a.xs_l, ir, a.is_c, a.is_l, H, t0 - H + j, va, vb);
+
+  unsigned k = 0;
+  for (i64 t = t0; t < t1; t += kTL, ++k) {
+    const unsigned s = k % NS, use = k / NS;
+    if (!mbar_wait(&full[s], use & 1)) return;
+    float xa[8], xb[8];
+    lds8<T>(smem + s * TB, 2 * warp, lane, xa);
+    lds8<T>(smem + s * TB, 2 * warp + 1, lane, xb);
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[s]);
+    float2 xp[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) xp[i] = f2(xa[i], xb[i]);
+    float2 h[H];
+#pragma unroll
+    for (int j = 0; j < H; ++j) {
+      const float2 up = shfl_up2(xp[8 - H + j], 1);
+      const float2 nc = shfl2(xp[8 - H + j], 31);
+      h[j] = lane == 0 ? carry[j] : up;
+      carry[j] = nc;
+    }
+    float oa8[8], ob8[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      float2 acc = bp;
+#pragma unroll
+      for (int kk = 0; kk < W; ++kk) {
+        const int q = i - H + kk;
+        acc = fma2(wp[kk], q >= 0 ? xp[q >= 0 ? q : 0] : h[q >= 0 ? 0 : q + H], acc);
+      }
+      if (SILU) acc = silu2(acc);
+      oa8[i] = acc.x;
+      ob8[i] = acc.y;
+    }
+    const i64 pos = t + 8 * lane;
+    if (pos < t1) {
+      if (va) stg8<T>(oa + pos, oa8);
+      if (vb) stg8<T>(oa + a.os_c + pos, ob8);
+    }
+  }
+  if (a.fin != nullptr && t1 == a.L && lane < H) {
+    T* f = static_cast<T*>(a.fin) + b * a.fs_b + ra * a.fs_c + lane * a.fs_l;
+    const i64 q = a.L - H + lane;
+    const float2 v = xc_pair(xr, a.xs_c, a.xs_l, ir, a.is_c, a.is_l, H, q, va, vb);
+    if (va) f[0] = Cvt<T>::to(v.x);
+    if (vb) f[a.fs_c] = Cvt<T>::to(v.y);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Backward
+// ---------------------------------------------------------------------------
+
+// dx of the 8 positions of a lane from dpre of those positions (d) and of the
+// H positions after them (rh), plus dfinal where final_states read them.
+template <typename T, int W>
+__device__ __forceinline__ void emit_dx(const float2 (&d)[8], const float2 (&rh)[W - 1], const float2 (&wp)[W],
+                                        i64 pos, i64 t1, const BwdArgs& a, T* dxa, const T* fa, bool va, bool vb) {
+  constexpr int H = W - 1;
+  float ea[8], eb[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    float2 acc = f2(0.f, 0.f);
+#pragma unroll
+    for (int m = 0; m <= H; ++m) {
+      const int q = i + m;
+      acc = fma2(wp[H - m], q < 8 ? d[q < 8 ? q : 0] : rh[q < 8 ? 0 : q - 8], acc);
+    }
+    if (fa != nullptr) {
+      const i64 qf = pos + i + H - a.L;
+      if (qf >= 0 && pos + i < a.L) {
+        if (va) acc.x += Cvt<T>::f(fa[qf * a.fs_l]);
+        if (vb) acc.y += Cvt<T>::f(fa[a.fs_c + qf * a.fs_l]);
+      }
+    }
+    ea[i] = acc.x;
+    eb[i] = acc.y;
+  }
+  if (pos < t1) {
+    if (va) stg8<T>(dxa + pos, ea);
+    if (vb) stg8<T>(dxa + a.dxs_c + pos, eb);
+  }
+}
+
+template <typename T, int W, bool SILU>
+__global__ void __launch_bounds__(kThreadsSeq) bwd_seq_tma_kernel(const __grid_constant__ SeqBwdParams p) {
+  constexpr int H = W - 1;
+  constexpr unsigned TB = seq_tile_bytes<T>();
+  constexpr unsigned SB = 2 * TB;
+  constexpr int NS = seq_bwd_stages<T>();
+  extern __shared__ __align__(128) unsigned char smem[];
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + NS * SB);
+  uint64_t* empty = full + NS;
+  const BwdArgs& a = p.a;
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const i64 item = blockIdx.x;
+  const i64 seg = item % a.nseg;
+  const i64 rest = item / a.nseg;
+  const i64 grp = rest % p.groups;
+  const i64 b = rest / p.groups;
+  const i64 c0 = grp * kRows;
+  const i64 t0 = seg * a.seg_len;
+  const i64 t1 = min(a.L, t0 + a.seg_len);
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < NS; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], kSW);
+    }
+    fence_mbar_init();
+  }
+  __syncthreads();
+
+  if (warp == kSW) {
+    if (lane == 0) {
+      prefetch_tensormap(&p.map_x);
+      prefetch_tensormap(&p.map_g);
+      unsigned k = 0;
+      for (i64 t = t0; t < t1; t += kTL, ++k) {
+        const unsigned s = k % NS, use = k / NS;
+        if (use > 0 && !mbar_wait(&empty[s], (use - 1) & 1)) return;
+        mbar_arrive_expect_tx(&full[s], SB);
+        tma_load_3d(smem + s * SB, &p.map_x, &full[s], (int)t, (int)c0, (int)b);
+        tma_load_3d(smem + s * SB + TB, &p.map_g, &full[s], (int)t, (int)c0, (int)b);
+      }
+    }
+    return;
+  }
+
+  const i64 ra = c0 + 2 * warp;
+  const bool va = ra < a.D, vb = ra + 1 < a.D;
+  const T* __restrict__ wt = static_cast<const T*>(a.w);
+  const T* __restrict__ bias = static_cast<const T*>(a.bias);
+  float2 wp[W];
+#pragma unroll
+  for (int k = 0; k < W; ++k)
+    wp[k] = f2(va ? Cvt<T>::f(wt[ra * a.ws_c + k * a.ws_k]) : 0.f, vb ? Cvt<T>::f(wt[(ra + 1) * a.ws_c + k * a.ws_k]) : 0.f);
+  const float2 bp = f2((bias && va) ? Cvt<T>::f(bias[ra * a.bs]) : 0.f, (bias && vb) ? Cvt<T>::f(bias[(ra + 1) * a.bs]) : 0.f);
+  const T* __restrict__ xr = static_cast<const T*>(a.x) + b * a.xs_b + ra * a.xs_c;
+  const T* __restrict__ gr = static_cast<const T*>(a.dout) + b * a.gs_b + ra * a.gs_c;
+  const T* __restrict__ ir = a.init ? static_cast<const T*>(a.init) + b * a.is_b + ra * a.is_c : nullptr;
+  const T* __restrict__ fa = a.dfin ? static_cast<const T*>(a.dfin) + b * a.fs_b + ra * a.fs_c : nullptr;
+  T* __restrict__ dxa = static_cast<T*>(a.dx) + b * a.dxs_b + ra * a.dxs_c;
+
+  float2 carry[H];
+#pragma unroll
+  for (int j = 0; j < H; ++j) carry[j] = xc_pair(xr, a.xs_c, a.xs_l, ir, a.is_c, a.is_l, H, t0 - H + j, va, vb);
+  // dpre just past the segment (0 past the sequence), for lane 31's last dx.
+  float2 rend[H];
+#pragma unroll
+  for (int j = 0; j < H; ++j) {
+    const i64 q = t1 + j;
+    rend[j] = f2(0.f, 0.f);
+    if (q < a.L) {
+      float2 pre = bp;
+#pragma unroll
+      for (int kk = 0; kk < W; ++kk)
+        pre = fma2(wp[kk], xc_pair(xr, a.xs_c, a.xs_l, ir, a.is_c, a.is_l, H, q - H + kk, va, vb), pre);
+      const float2 g = f2(va ? Cvt<T>::f(gr[q * a.gs_l]) : 0.f, vb ? Cvt<T>::f(gr[a.gs_c + q * a.gs_l]) : 0.f);
+      rend[j] = SILU ? mul2(g, silu_grad2(pre)) : g;
+    }
+  }
+
+  float2 dw[W];
+#pragma unroll
+  for (int k = 0; k < W; ++k) dw[k] = f2(0.f, 0.f);
+  float2 db = f2(0.f, 0.f);
+  float2 dprev[8];
+  i64 tprev = -1;
+
+  unsigned k = 0;
+  for (i64 t = t0; t < t1; t += kTL, ++k) {
+    const unsigned s = k % NS, use = k / NS;
+    if (!mbar_wait(&full[s], use & 1)) return;
+    float xa[8], xb[8], ga[8], gb[8];
+    lds8<T>(smem + s * SB, 2 * warp, lane, xa);
+    lds8<T>(smem + s * SB, 2 * warp + 1, lane, xb);
+    lds8<T>(smem + s * SB + TB, 2 * warp, lane, ga);
+    lds8<T>(smem + s * SB + TB, 2 * warp + 1, lane, gb);
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[s]);
+    float2 xp[8], d[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) xp[i] = f2(xa[i], xb[i]);
+    float2 h[H];
+#pragma unroll
+    for (int j = 0; j < H; ++j) {
+      const float2 up = shfl_up2(xp[8 - H + j], 1);
+      const float2 nc = shfl2(xp[8 - H + j], 31);
+      h[j] = lane == 0 ? carry[j] : up;
+      carry[j] = nc;
+    }
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      float2 pre = bp;
+#pragma unroll
+      for (int kk = 0; kk < W; ++kk) {
+        const int q = i - H + kk;
+        pre = fma2(wp[kk], q >= 0 ? xp[q >= 0 ? q : 0] : h[q >= 0 ? 0 : q + H], pre);
+      }
+      const float2 g = f2(ga[i], gb[i]);
+      d[i] = SILU ? mul2(g, silu_grad2(pre)) : g;
+      db = add2(db, d[i]);
+#pragma unroll
+      for (int kk = 0; kk < W; ++kk) {
+        const int q = i - H + kk;
+        dw[kk] = fma2(d[i], q >= 0 ? xp[q >= 0 ? q : 0] : h[q >= 0 ? 0 : q + H], dw[kk]);
+      }
+    }
+    // dx of the previous tile: lane 31 now has its right halo (this tile's
+    // first dpre values, from lane 0).
+    if (tprev >= 0) {
+      float2 rh[H];
+#pragma unroll
+      for (int j = 0; j < H; ++j) {
+        const float2 nxt = shfl_down2(dprev[j], 1);
+        const float2 first = shfl2(d[j], 0);
+        rh[j] = lane == 31 ? first : nxt;
+      }
+      emit_dx<T, W>(dprev, rh, wp, tprev + 8 * lane, t1, a, dxa, fa, va, vb);
+    }
+    // dinitial_states: dpre of positions 0 .. H-1 live in lane 0 of tile 0.
+    if (t == 0 && lane == 0 && a.dinit != nullptr) {
+      T* di = static_cast<T*>(a.dinit) + b * a.dis_b + ra * a.dis_c;
+#pragma unroll
+      for (int i = 0; i < H; ++i) {
+        float2 acc = f2(0.f, 0.f);
+#pragma unroll
+        for (int kk = 0; kk <= i; ++kk) acc = fma2(wp[kk], d[i - kk], acc);
+        if (fa != nullptr && i - a.L >= 0) {
+          if (va) acc.x += Cvt<T>::f(fa[(i - a.L) * a.fs_l]);
+          if (vb) acc.y += Cvt<T>::f(fa[a.fs_c + (i - a.L) * a.fs_l]);
+        }
+        if (va) di[i * a.dis_l] = Cvt<T>::to(acc.x);
+        if (vb) di[a.dis_c + i * a.dis_l] = Cvt<T>::to(acc.y);
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < 8; ++i) dprev[i] = d[i];
+    tprev = t;
+  }
+  if (tprev >= 0) {
+    float2 rh[H];
+#pragma unroll
+    for (int j = 0; j < H; ++j) {
+      const float2 nxt = shfl_down2(dprev[j], 1);
+      rh[j] = lane == 31 ? rend[j] : nxt;
+    }
+    emit_dx<T, W>(dprev, rh, wp, tprev + 8 * lane, t1, a, dxa, fa, va, vb);
+  }
+  // Warp sums of the dweight / dbias partials; lane 0 writes this item's slot.
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) {
+#pragma unroll
+    for (int kk = 0; kk < W; ++kk) dw[kk] = add2(dw[kk], shfl_down2(dw[kk], off));
+    db = add2(db, shfl_down2(db, off));
+  }
+  if (lane == 0) {
+    float* pp = a.partials + ((b * a.nseg + seg) * a.D + ra) * (W + 1);
+    if (va) {
+#pragma unroll
+      for (int kk = 0; kk < W; ++kk) pp[kk] = dw[kk].x;
+      pp[W] = db.x;
+    }
+    if (vb) {
+#pragma unroll
+      for (int kk = 0; kk < W; ++kk) pp[W + 1 + kk] = dw[kk].y;
+      pp[W + 1 + W] = db.y;
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Host side
+// ---------------------------------------------------------------------------
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static std::atomic<void*> fn{nullptr};
+  void* f = fn.load(std::memory_order_acquire);
+  if (f == nullptr) {
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess || f == nullptr)
+      return nullptr;
+    fn.store(f, std::memory_order_release);
+  }
+  return reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(f);
+}
+
+template <typename T>
+CUtensorMapDataType tma_dtype() {
+  if (sizeof(T) == 4) return CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
+  if (std::is_same<T, __half>::value) return CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  return CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+}
+
+// 3-D map over the (L, D, B) view of a seqlen-contiguous tensor; box
+// (256 positions, 8 channels, 1), zero fill outside.
+template <typename T>
+bool make_seq_map(CUtensorMap* m, const void* base, i64 L, i64 D, i64 B, i64 s_c, i64 s_b) {
+  PFN_cuTensorMapEncodeTiled_v12000 enc = encode_fn();
+  if (enc == nullptr) return false;
+  const i64 esz = sizeof(T);
+  if (D == 1) s_c = L;
+  if (B == 1) s_b = D * s_c;
+  cuuint64_t dims[3] = {(cuuint64_t)L, (cuuint64_t)D, (cuuint64_t)B};
+  cuuint64_t strides[2] = {(cuuint64_t)(s_c * esz), (cuuint64_t)(s_b * esz)};
+  cuuint32_t box[3] = {(cuuint32_t)kTL, (cuuint32_t)kRows, 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  return enc(m, tma_dtype<T>(), 3, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+             CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+bool aligned_to(const void* p, int bytes) { return (reinterpret_cast<uintptr_t>(p) % (uintptr_t)bytes) == 0; }
+
+// Unit seqlen stride, 16-byte aligned base and channel / batch pitches.
+bool seq_tensor_ok(const void* base, i64 s_c, i64 s_l, i64 s_b, i64 B, i64 D, int esz) {
+  return base != nullptr && s_l == 1 && aligned_to(base, 16) && (D == 1 || ((s_c * esz) % 16 == 0 && s_c > 0)) &&
+         (B == 1 || ((s_b * esz) % 16 == 0 && s_b > 0)) && (s_c * esz) < (1LL << 40) && (s_b * esz) < (1LL << 40);
+}
+
+bool seq_shape_ok(i64 B, i64 D, i64 L) {
+  return B >= 1 && D >= 1 && L >= 8 && L % 8 == 0 && L < (1LL << 31) && D < (1LL << 31) && B < (1LL << 31);
+}
+
+int esize(int dtype) { return dtype == 2 ? 4 : 2; }
+
+template <typename K>
+cudaError_t prepare(K kernel, size_t smem, std::atomic<int>& attr_done, std::atomic<int>& occ, int* nb) {
+  if (!attr_done.load(std::memory_order_acquire)) {
+    cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+    attr_done.store(1, std::memory_order_release);
+  }
+  return blocks_per_sm(kernel, kThreadsSeq, smem, occ, nb);
+}
+
+// Items = (batch, group of 8 channels, segment); segments split long rows
+// when there are too few (batch, group) pairs to fill the GPU.
+void seq_schedule(const DeviceInfo& dev, int nb, i64 B, i64 D, i64 L, Plan* plan) {
+  const i64 groups = ceil_div(D, (i64)kRows);
+  const i64 pairs = B * groups;
+  const i64 target = 2 * (i64)dev.sms * nb;
+  i64 nseg = 1;
+  if (pairs < target) nseg = std::min<i64>(ceil_div(target, pairs), ceil_div(L, (i64)kTL));
+  if (nseg < 1) nseg = 1;
+  const i64 seg_len = ceil_div(ceil_div(L, nseg), (i64)kTL) * kTL;
+  nseg = ceil_div(L, seg_len);
+  plan->layout = kSeq;
+  plan->vec = true;
+  plan->threads = kThreadsSeq;
+  plan->groups = groups;
+  plan->nseg = nseg;
+  plan->seg_len = seg_len;
+  plan->n_items = pairs * nseg;
+  plan->grid = pairs * nseg;
+  plan->n_partials = B * nseg;
+}
+
+template <typename T, int W, bool SILU>
+cudaError_t seq_fwd_instance(SeqFwdParams* prm, const Plan* plan, cudaStream_t stream, int* nb_out) {
+  constexpr size_t smem = (size_t)seq_fwd_stages<T>() * seq_tile_bytes<T>() + 2 * seq_fwd_stages<T>() * sizeof(uint64_t);
+  static std::atomic<int> attr{0}, occ{0};
+  int nb = 1;
+  cudaError_t e = prepare(fwd_seq_tma_kernel<T, W, SILU>, smem, attr, occ, &nb);
+  if (e != cudaSuccess) return e;
+  if (nb_out) *nb_out = nb;
+  if (prm == nullptr) return cudaSuccess;
+  fwd_seq_tma_kernel<T, W, SILU><<<(unsigned)plan->grid, kThreadsSeq, smem, stream>>>(*prm);
+  return cudaGetLastError();
+}
+
+template <typename T, int W, bool SILU>
+cudaError_t seq_bwd_instance(SeqBwdParams* prm, const Plan* plan, cudaStream_t stream, int* nb_out) {
+  constexpr size_t smem =
+      (size_t)seq_bwd_stages<T>() * 2 * seq_tile_bytes<T>() + 2 * seq_bwd_stages<T>() * sizeof(uint64_t);
+  static std::atomic<int> attr{0}, occ{0};
+  int nb = 1;
+  cudaError_t e = prepare(bwd_seq_tma_kernel<T, W, SILU>, smem, attr, occ, &nb);
+  if (e != cudaSuccess) return e;
+  if (nb_out) *nb_out = nb;
+  if (prm == nullptr) return cudaSuccess;
+  bwd_seq_tma_kernel<T, W, SILU><<<(unsigned)plan->grid, kThreadsSeq, smem, stream>>>(*prm);
+  return cudaGetLastError();
+}
+
+struct SeqFwdOp {
+  const FwdArgs& a;
+  Plan* plan;
+  cudaStream_t stream;
+  bool launch;
+  template <typename T, int W>
+  cudaError_t operator()() {
+    const bool silu = a.silu != 0;
+    SeqFwdParams* prm = nullptr;
+    SeqFwdParams storage;
+    if (launch) {
+      storage.a = a;
+      storage.a.nseg = plan->nseg;
+      storage.a.seg_len = plan->seg_len;
+      storage.groups = plan->groups;
+      if (!make_seq_map<T>(&storage.map_x, a.x, a.L, a.D, a.B, a.xs_c, a.xs_b)) return cudaErrorInvalidValue;
+      prm = &storage;
+    }
+    int nb = 1;
+    cudaError_t e = silu ? seq_fwd_instance<T, W, true>(prm, plan, stream, &nb)
+                         : seq_fwd_instance<T, W, false>(prm, plan, stream, &nb);
+    if (e != cudaSuccess || launch) return e;
+    DeviceInfo dev;
+    e = device_info(&dev);
+    if (e != cudaSuccess) return e;
+    seq_schedule(dev, nb, a.B, a.D, a.L, plan);
+    plan->n_partials = 0;
+    return cudaSuccess;
+  }
+};
+
+struct SeqBwdOp {
+  const BwdArgs& a;
+  Plan* plan;
+  cudaStream_t stream;
+  bool launch;
+  template <typename T, int W>
+  cudaError_t operator()() {
+    const bool silu = a.silu != 0;
+    SeqBwdParams* prm = nullptr;
+    SeqBwdParams storage;
+    if (launch) {
+      storage.a = a;
+      storage.a.nseg = plan->nseg;
+      storage.a.seg_len = plan->seg_len;
+      storage.groups = plan->groups;
+      if (!make_seq_map<T>(&storage.map_x, a.x, a.L, a.D, a.B, a.xs_c, a.xs_b) ||
+          !make_seq_map<T>(&storage.map_g, a.dout, a.L, a.D, a.B, a.gs_c, a.gs_b))
+        return cudaErrorInvalidValue;
+      prm = &storage;
+    }
+    int nb = 1;
+    cudaError_t e = silu ? seq_bwd_instance<T, W, true>(prm, plan, stream, &nb)
+                         : seq_bwd_instance<T, W, false>(prm, plan, stream, &nb);
+    if (e != cudaSuccess || launch) return e;
+    DeviceInfo dev;
+    e = device_info(&dev);
+    if (e != cudaSuccess) return e;
+    seq_schedule(dev, nb, a.B, a.D, a.L, plan);
+    return cudaSuccess;
+  }
+};
+
+}  // namespace
+
+bool fwd_seq_tma_eligible(int dtype, const FwdArgs& a) {
+  const int esz = esize(dtype);
+  return a.seq == nullptr && seq_shape_ok(a.B, a.D, a.L) && encode_fn() != nullptr &&
+         seq_tensor_ok(a.x, a.xs_c, a.xs_l, a.xs_b, a.B, a.D, esz) &&
+         seq_tensor_ok(a.out, a.os_c, a.os_l, a.os_b, a.B, a.D, esz);
+}
+
+bool bwd_seq_tma_eligible(int dtype, const BwdArgs& a) {
+  const int esz = esize(dtype);
+  return a.seq == nullptr && seq_shape_ok(a.B, a.D, a.L) && encode_fn() != nullptr &&
+         seq_tensor_ok(a.x, a.xs_c, a.xs_l, a.xs_b, a.B, a.D, esz) &&
+         seq_tensor_ok(a.dout, a.gs_c, a.gs_l, a.gs_b, a.B, a.D, esz) &&
+         seq_tensor_ok(a.dx, a.dxs_c, a.dxs_l, a.dxs_b, a.B, a.D, esz);
+}
+
+cudaError_t plan_fwd_seq_tma(int dtype, int width, const FwdArgs& a, Plan* plan) {
+  return dispatch(dtype, width, SeqFwdOp{a, plan, nullptr, false});
+}
+
+cudaError_t launch_fwd_seq_tma(int dtype, int width, const FwdArgs& a, const Plan& plan, cudaStream_t stream) {
+  Plan p = plan;
+  return dispatch(dtype, width, SeqFwdOp{a, &p, stream, true});
+}
+
+cudaError_t plan_bwd_seq_tma(int dtype, int width, const BwdArgs& a, Plan* plan) {
+  return dispatch(dtype, width, SeqBwdOp{a, plan, nullptr, false});
+}
+
+cudaError_t launch_bwd_seq_tma(int dtype, int width, const BwdArgs& a, const Plan& plan, cudaStream_t stream) {
+  Plan p = plan;
+  return dispatch(dtype, width, SeqBwdOp{a, &p, stream, true});
+}
+
+cudaError_t read_seq_wait_timeouts(unsigned* count) { return tu_read_wait_timeouts(count); }
+
+}  // namespace cc1d

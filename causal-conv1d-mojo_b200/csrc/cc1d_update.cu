@@ -101,6 +101,196 @@ __global__ void __launch_bounds__(128) update_kernel(const UpdateArgs a) {
   }
 }
 
+// Fast path of the linear decode step for the common serving layout: one new
+// token (L == 1), conv_state rows contiguous (stride 1 over state_len, state_len
+// elements per channel), weights (D, W) contiguous, x/out with unit channel
+// stride, 16-byte aligned rows, D % 8 == 0.  A thread owns 8 adjacent channels
+// of one batch row: x, bias, the weights and (linear mode) the state rows are
+// read as 16-byte vectors, all before any store, so a block has two dependent
+// memory round trips (the pool index, then everything else) and the grid is
+// about half a wave at the serving shapes.
+// Linear mode with state_len == W-1: new state = [old[1..W-2], x].
+template <typename T, int W, bool CIRC>
+__global__ void __launch_bounds__(128) update_vec_kernel(const UpdateArgs a) {
+  constexpr int H = W - 1;
+  constexpr int V = 8;  // channels per thread
+  typedef Pack<T, 16 / sizeof(T)> P16;
+  constexpr int E16 = 16 / sizeof(T);  // elements per 16-byte vector
+  const i64 groups = a.D / V;
+  const i64 cblocks = ceil_div(groups, (i64)blockDim.x);
+  const i64 b = blockIdx.x / cblocks;
+  const i64 g = (blockIdx.x - b * cblocks) * blockDim.x + threadIdx.x;
+  if (g >= groups) return;
+  const i64 c0 = g * V;
+  T* __restrict__ ob = static_cast<T*>(a.out) + b * a.os_b + c0;
+  i64 row = b;
+  if (a.idx != nullptr) {
+    const int r = a.idx[b];
+    if (r < 0 || r >= a.state_rows) {
+      P16 z;
+#pragma unroll
+      for (int i = 0; i < E16; ++i) z.v[i] = Cvt<T>::to(0.f);
+#pragma unroll
+      for (int i = 0; i < V; i += E16) st_pack<T, E16>(ob + i, z);
+      return;
+    }
+    row = r;
+  }
+  T* __restrict__ st = static_cast<T*>(a.state) + row * a.ss_b + c0 * a.S;
+  // Loads: x, bias, weights, state -- all independent.
+  T xv[V], bv[V], wv[V * W], sv[V * H];
+#pragma unroll
+  for (int i = 0; i < V; i += E16) {
+    const P16 px = ld_pack<T, E16>(static_cast<const T*>(a.x) + b * a.xs_b + c0 + i);
+#pragma unroll
+    for (int e = 0; e < E16; ++e) xv[i + e] = px.v[e];
+  }
+  if (a.bias != nullptr) {
+#pragma unroll
+    for (int i = 0; i < V; i += E16) {
+      const P16 pb = ld_pack<T, E16>(static_cast<const T*>(a.bias) + c0 + i);
+#pragma unroll
+      for (int e = 0; e < E16; ++e) bv[i + e] = pb.v[e];
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < V; ++i) bv[i] = Cvt<T>::to(0.f);
+  }
+#pragma unroll
+  for (int i = 0; i < V * W; i += E16) {
+    const P16 pw = ld_pack<T, E16>(static_cast<const T*>(a.w) + c0 * W + i);
+#pragma unroll
+    for (int e = 0; e < E16; ++e) wv[i + e] = pw.v[e];
+  }
+  i64 head = 0;
+  if (CIRC) {
+    i64 cs = (i64)a.cache_seqlens[b] % a.S;
+    if (cs < 0) cs += a.S;
+    head = cs;
+    i64 ui = cs - H;
+    if (ui < 0) ui += a.S;
+#pragma unroll
+    for (int j = 0; j < H; ++j) {
+#pragma unroll
+      for (int v = 0; v < V; ++v) sv[v * H + j] = st[v * a.S + ui];
+      ui = (ui + 1 == a.S) ? 0 : ui + 1;
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < V * H; i += E16) {
+      const P16 ps = ld_pack<T, E16>(st + i);
+#pragma unroll
+      for (int e = 0; e < E16; ++e) sv[i + e] = ps.v[e];
+    }
+  }
+  // Compute (same tap order and SiLU as every other kernel).
+  P16 po[V / E16 > 0 ? V / E16 : 1];
+#pragma unroll
+  for (int v = 0; v < V; ++v) {
+    float acc = Cvt<T>::f(bv[v]);
+#pragma unroll
+    for (int k = 0; k < H; ++k) acc = fmaf(Cvt<T>::f(wv[v * W + k]), Cvt<T>::f(sv[v * H + k]), acc);
+    acc = fmaf(Cvt<T>::f(wv[v * W + H]), Cvt<T>::f(xv[v]), acc);
+    if (a.silu) acc = silu_f(acc);
+    po[v / E16].v[v % E16] = Cvt<T>::to(acc);
+  }
+  // Stores.
+#pragma unroll
+  for (int i = 0; i < V; i += E16) st_pack<T, E16>(ob + i, po[i / E16]);
+  if (CIRC) {
+#pragma unroll
+    for (int v = 0; v < V; ++v) st[v * a.S + head] = xv[v];
+  } else {
+    // New rows [old[1..H-1], x] for the V channels, packed back to vectors.
+    T nv[V * H];
+#pragma unroll
+    for (int v = 0; v < V; ++v) {
+#pragma unroll
+      for (int j = 0; j < H - 1; ++j) nv[v * H + j] = sv[v * H + j + 1];
+      nv[v * H + H - 1] = xv[v];
+    }
+#pragma unroll
+    for (int i = 0; i < V * H; i += E16) {
+      P16 pn;
+#pragma unroll
+      for (int e = 0; e < E16; ++e) pn.v[e] = nv[i + e];
+      st_pack<T, E16>(st + i, pn);
+    }
+  }
+}
+
+// Single-token circular-buffer decode (any strides, any state_len).  A warp
+// owns 256 channels of one batch row, lane l the channels l + 32*v (v < 8), so
+// every warp-wide access touches 32 consecutive channel rows.  All loads of a
+// thread's 8 channels are issued before any store (no read-after-write
+// ordering between channels), so the grid is about half a wave at the
+// serving shapes with two dependent memory round trips per block.
+template <typename T, int W>
+__global__ void __launch_bounds__(128) update_circ_kernel(const UpdateArgs a) {
+  constexpr int H = W - 1;
+  constexpr int V = 8;
+  constexpr int CHUNK = 128 * V;  // channels per block (4 warps x 256)
+  const i64 chunks = ceil_div(a.D, (i64)CHUNK);
+  const i64 b = blockIdx.x / chunks;
+  const i64 cbase = (blockIdx.x - b * chunks) * CHUNK + (threadIdx.x >> 5) * 256 + (threadIdx.x & 31);
+  const T* __restrict__ x = static_cast<const T*>(a.x);
+  const T* __restrict__ wt = static_cast<const T*>(a.w);
+  const T* __restrict__ bias = static_cast<const T*>(a.bias);
+  T* __restrict__ out = static_cast<T*>(a.out);
+  i64 row = b;
+  if (a.idx != nullptr) {
+    const int r = a.idx[b];
+    if (r < 0 || r >= a.state_rows) {
+#pragma unroll
+      for (int v = 0; v < V; ++v) {
+        const i64 c = cbase + 32 * v;
+        if (c < a.D) out[b * a.os_b + c * a.os_c] = Cvt<T>::to(0.f);
+      }
+      return;
+    }
+    row = r;
+  }
+  T* __restrict__ st = static_cast<T*>(a.state) + row * a.ss_b;
+  i64 cs = (i64)a.cache_seqlens[b] % a.S;
+  if (cs < 0) cs += a.S;
+  i64 pos[H];
+  {
+    i64 ui = cs - H;
+    if (ui < 0) ui += a.S;
+#pragma unroll
+    for (int j = 0; j < H; ++j) {
+      pos[j] = ui * a.ss_l;
+      ui = (ui + 1 == a.S) ? 0 : ui + 1;
+    }
+  }
+  T xv[V];
+  float acc[V];
+#pragma unroll
+  for (int v = 0; v < V; ++v) {
+    const i64 c = cbase + 32 * v;
+    acc[v] = 0.f;
+    xv[v] = Cvt<T>::to(0.f);
+    if (c < a.D) {
+      xv[v] = x[b * a.xs_b + c * a.xs_c];
+      acc[v] = bias ? Cvt<T>::f(bias[c * a.bs]) : 0.f;
+      const T* sc = st + c * a.ss_c;
+#pragma unroll
+      for (int k = 0; k < H; ++k) acc[v] = fmaf(Cvt<T>::f(wt[c * a.ws_c + k * a.ws_k]), Cvt<T>::f(sc[pos[k]]), acc[v]);
+      acc[v] = fmaf(Cvt<T>::f(wt[c * a.ws_c + H * a.ws_k]), Cvt<T>::f(xv[v]), acc[v]);
+    }
+  }
+#pragma unroll
+  for (int v = 0; v < V; ++v) {
+    const i64 c = cbase + 32 * v;
+    if (c < a.D) {
+      float o = acc[v];
+      if (a.silu) o = silu_f(o);
+      out[b * a.os_b + c * a.os_c] = Cvt<T>::to(o);
+      st[c * a.ss_c + cs * a.ss_l] = xv[v];
+    }
+  }
+}
+
 template <typename T>
 __global__ void varlen_states_kernel(const VarlenArgs a) {
   const i64 n = a.B * a.S * a.D;
@@ -137,12 +327,37 @@ cudaError_t dispatch_update_width(int width, F&& f) {
   }
 }
 
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// Conditions of update_vec_kernel (see its comment).
+template <typename T, int W>
+bool vec_path_ok(const UpdateArgs& a) {
+  const i64 e = 16 / (i64)sizeof(T);  // elements per 16 bytes
+  return a.cache_seqlens == nullptr && a.L == 1 && a.D % 8 == 0 && a.S == W - 1 && a.ss_l == 1 && a.ss_c == a.S &&
+         aligned16(a.state) && (a.ss_b % e == 0) && ((8 * a.S) % e == 0) && a.ws_k == 1 && a.ws_c == W &&
+         aligned16(a.w) && (8 * W) % e == 0 && a.xs_c == 1 && aligned16(a.x) && (a.B == 1 || a.xs_b % e == 0) &&
+         a.os_c == 1 && aligned16(a.out) && (a.B == 1 || a.os_b % e == 0) &&
+         (a.bias == nullptr || (a.bs == 1 && aligned16(a.bias)));
+}
+
 struct LaunchUpdate {
   const UpdateArgs& a;
   cudaStream_t stream;
   template <typename T, int W>
   cudaError_t operator()() {
     const int threads = 128;
+    if (vec_path_ok<T, W>(a)) {
+      const i64 blocks = ceil_div(a.D / 8, (i64)threads) * a.B;
+      if (blocks > 0x7fffffffLL) return cudaErrorInvalidConfiguration;
+      update_vec_kernel<T, W, false><<<(unsigned)blocks, threads, 0, stream>>>(a);
+      return cudaGetLastError();
+    }
+    if (a.cache_seqlens != nullptr && a.L == 1) {
+      const i64 blocks = ceil_div(a.D, (i64)threads * 8) * a.B;
+      if (blocks > 0x7fffffffLL) return cudaErrorInvalidConfiguration;
+      update_circ_kernel<T, W><<<(unsigned)blocks, threads, 0, stream>>>(a);
+      return cudaGetLastError();
+    }
     const i64 blocks = ceil_div(a.D, (i64)threads) * a.B;
     if (blocks > 0x7fffffffLL) return cudaErrorInvalidConfiguration;
     update_kernel<T, W><<<(unsigned)blocks, threads, 0, stream>>>(a);

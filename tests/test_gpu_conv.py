@@ -134,7 +134,7 @@ def test_sweep_vs_oracle(shape, dtype, W, layout):
 @pytest.mark.parametrize("layout", ["contig", "chanlast", "strided"])
 @pytest.mark.parametrize("W", [2, 4])
 @pytest.mark.parametrize("dtype", ["fp32", "bf16"])
-@pytest.mark.parametrize("L", [1, 2, 3, 5, 300, 2100])
+@pytest.mark.parametrize("L", [1, 2, 3, 5, 300, 2100, 4096])
 def test_states_vs_oracle(L, dtype, W, layout):
     dt = DTYPES[dtype]
     B, D = 2, 72

@@ -44,12 +44,13 @@ def test_golden(golden, case, two_d):
     assert_bitwise(state.cpu(), exp["conv_state"].to(dt), "conv_state")
 
 
+@pytest.mark.parametrize("D", [300, 512])  # 512: the vectorised single-token path
 @pytest.mark.parametrize("mode", ["linear", "circular", "pool", "pool_circular"])
-@pytest.mark.parametrize("W", [2, 4, 7])
+@pytest.mark.parametrize("W", [2, 4, 7, 9])
 @pytest.mark.parametrize("dtype", ["fp32", "bf16", "fp16"])
-def test_vs_oracle(dtype, W, mode):
+def test_vs_oracle(dtype, W, mode, D):
     dt = DTYPES[dtype]
-    B, D, L = 9, 300, 1 if W != 7 else 3
+    B, L = 9, 1 if W != 7 else 3
     S = W - 1 if mode in ("linear", "pool") else W + 6
     rows = B if mode in ("linear", "circular") else 2 * B + 1
     x = seeded((B, D, L), dt, W)
