@@ -498,6 +498,81 @@ def run_reference(args):
     return 0
 
 
+def run_only(args):
+    """Launch one op of one config `args.reps` times (for profilers); prints
+    the average CUDA-event time per launch."""
+    from causal_conv1d_b200 import _ops
+
+    torch.cuda.set_device(0)
+    g = torch.Generator(device="cuda").manual_seed(5)
+
+    def rn(*s, dt=DT):
+        return torch.randn(*s, generator=g, device="cuda", dtype=torch.float32).to(dt)
+
+    def ru(*s, dt=DT):
+        return (torch.rand(*s, generator=g, device="cuda", dtype=torch.float32) - 0.5).to(dt)
+
+    op = args.only
+    if op in ("fwd_c2", "bwd_c2"):
+        x, w, b, init, dout = make_c2(0, "cuda")
+        out, fs, dx = torch.empty_like(x), torch.empty_like(init), torch.empty_like(x)
+        dwdb = torch.empty(D * (W + 1), dtype=torch.float32, device="cuda")
+        dw, db, dinit = torch.empty(D, W, dtype=DT, device="cuda"), torch.empty(D, dtype=DT, device="cuda"), \
+            torch.empty_like(init)
+        fn = (lambda: _ops.fwd(x, w, b, None, init, out, True, fs)) if op == "fwd_c2" else \
+            (lambda: _ops.bwd(x, w, b, dout, None, init, None, dx, dwdb, dinit, dw, db, True))
+    elif op in ("fwd_c5", "bwd_c5"):
+        B5, D5, L5 = args.c5_batch, 8192, 8192
+        x, dout = rn(B5, D5, L5), rn(B5, D5, L5)
+        w5, b5, init = ru(D5, W), ru(D5), rn(B5, D5, W - 1)
+        out, dx, fs, dinit = torch.empty_like(x), torch.empty_like(x), torch.empty_like(init), torch.empty_like(init)
+        dwdb = torch.empty(D5 * (W + 1), dtype=torch.float32, device="cuda")
+        dw, db = torch.empty(D5, W, dtype=DT, device="cuda"), torch.empty(D5, dtype=DT, device="cuda")
+        fn = (lambda: _ops.fwd(x, w5, b5, None, init, out, True, fs)) if op == "fwd_c5" else \
+            (lambda: _ops.bwd(x, w5, b5, dout, None, init, None, dx, dwdb, dinit, dw, db, True))
+    elif op in ("fwd_c4", "bwd_c4"):
+        dt = torch.float16
+        Lv, Dv = 65536, 4096
+        gl = torch.Generator().manual_seed(0)
+        raw = torch.randint(256, 4097, (32,), generator=gl)
+        lens = (raw * Lv // raw.sum()).clamp(min=1)
+        lens[-1] += Lv - lens.sum()
+        seq = torch.repeat_interleave(torch.arange(32, dtype=torch.int32), lens).view(1, Lv).cuda()
+        x, dout = rn(1, Lv, Dv, dt=dt).transpose(1, 2), rn(1, Lv, Dv, dt=dt).transpose(1, 2)
+        wv, bv = ru(Dv, W, dt=dt), ru(Dv, dt=dt)
+        out, dx = torch.empty_like(x), torch.empty_like(x)
+        dwdb = torch.empty(Dv * (W + 1), dtype=torch.float32, device="cuda")
+        dw, db = torch.empty(Dv, W, dtype=dt, device="cuda"), torch.empty(Dv, dtype=dt, device="cuda")
+        fn = (lambda: _ops.fwd(x, wv, bv, seq, None, out, True, None)) if op == "fwd_c4" else \
+            (lambda: _ops.bwd(x, wv, bv, dout, seq, None, None, dx, dwdb, None, dw, db, True))
+    elif op in ("update_c3a", "update_c3b"):
+        Bu, Du = 256, 5376
+        w, b = ru(Du, W), ru(Du)
+        x = rn(Bu, Du, 1)
+        out = torch.empty_like(x)
+        if op == "update_c3a":
+            pool = rn(512, Du, W - 1)
+            idx = torch.randperm(512, device="cuda")[:Bu].to(torch.int32)
+            fn = lambda: _ops.update(x, pool, w, b, None, idx, out, True)  # noqa: E731
+        else:
+            state = rn(Bu, Du, 8)
+            cache = torch.randint(0, 1024, (Bu,), device="cuda", dtype=torch.int32)
+            fn = lambda: _ops.update(x, state, w, b, cache, None, out, True)  # noqa: E731
+    else:
+        raise SystemExit(f"unknown op {op}")
+    for _ in range(args.warmup):
+        fn()
+    torch.cuda.synchronize()
+    a, c = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(args.reps):
+        fn()
+    c.record()
+    torch.cuda.synchronize()
+    print(json.dumps({"op": op, "reps": args.reps, "ms_per_launch_eager": a.elapsed_time(c) / args.reps}))
+    return 0
+
+
 def load_traffic():
     p = REPO / "profiles" / "ncu_traffic.json"
     if p.is_file():
@@ -517,9 +592,16 @@ def main():
     ap.add_argument("--skip-kernels", action="store_true", help="skip the secondary kernel table")
     ap.add_argument("--skip-e2e", action="store_true")
     ap.add_argument("--skip-cpu", action="store_true")
+    ap.add_argument("--only", default=None,
+                    help="launch one op alone (fwd_c2, bwd_c2, update_c3a, update_c3b, fwd_c4, bwd_c4, fwd_c5, "
+                         "bwd_c5) --reps times, for profilers; prints no contract line")
+    ap.add_argument("--reps", type=int, default=3)
+    ap.add_argument("--c5-batch", type=int, default=64, help="batch of the C5 shape in --only mode")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
+    if args.only:
+        return run_only(args)
     if args.impl == "reference":
         return run_reference(args)
 

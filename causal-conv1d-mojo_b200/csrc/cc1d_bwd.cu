@@ -491,17 +491,32 @@ __global__ void __launch_bounds__(kThreads) bwd_chan_kernel(const BwdArgs a) {
   }
 }
 
-// Sums the partial slots in slot order: dwdb[c*W+k] (dweight) and
-// dwdb[D*W+c] (dbias), plus optional dtype copies.
+// Sums the partial slots: a block owns 32 consecutive outputs (one per lane,
+// so every load is a coalesced 128-byte row segment); warp w adds slots
+// w, w+8, w+16, ... in order, then warp 0 adds the 8 warp sums in order.
+// The summation order depends only on the slot count, so results are
+// reproducible run to run.  Writes dwdb[c*W+k] (dweight) and dwdb[D*W+c]
+// (dbias), plus optional dtype copies.
+constexpr int kFinWarps = 8;
+
 template <typename T, int W>
-__global__ void finalize_kernel(const FinalizeArgs a) {
+__global__ void __launch_bounds__(kFinWarps * 32) finalize_kernel(const FinalizeArgs a) {
+  __shared__ float part[kFinWarps][32];
   const i64 n = a.D * (W + 1);
-  const i64 e = (i64)blockIdx.x * blockDim.x + threadIdx.x;
-  if (e >= n) return;
+  const int lane = threadIdx.x & 31;
+  const int warp = threadIdx.x >> 5;
+  const i64 e = (i64)blockIdx.x * 32 + lane;
+  float s = 0.f;
+  if (e < n)
+    for (i64 i = warp; i < a.n_partials; i += kFinWarps) s += a.partials[i * n + e];
+  part[warp][lane] = s;
+  __syncthreads();
+  if (warp != 0 || e >= n) return;
+  s = part[0][lane];
+#pragma unroll
+  for (int w2 = 1; w2 < kFinWarps; ++w2) s += part[w2][lane];
   const i64 c = e / (W + 1);
   const int k = (int)(e - c * (W + 1));
-  float s = 0.f;
-  for (i64 i = 0; i < a.n_partials; ++i) s += a.partials[i * n + e];
   if (k < W) {
     a.dwdb[c * W + k] = s;
     if (a.dw_out) static_cast<T*>(a.dw_out)[c * a.dws_c + k * a.dws_k] = Cvt<T>::to(s);
@@ -668,8 +683,7 @@ struct LaunchFinalize {
   cudaError_t operator()() {
     const i64 n = a.D * (W + 1);
     if (n == 0) return cudaSuccess;
-    const int threads = 256;
-    finalize_kernel<T, W><<<(unsigned)ceil_div(n, threads), threads, 0, stream>>>(a);
+    finalize_kernel<T, W><<<(unsigned)ceil_div(n, (i64)32), kFinWarps * 32, 0, stream>>>(a);
     return cudaGetLastError();
   }
 };

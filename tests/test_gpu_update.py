@@ -155,3 +155,30 @@ def test_varlen_random_vs_ref(dtype):
         got = causal_conv1d_varlen_states(x.to(DEV), cu.to(DEV), S).cpu()
         assert_bitwise(got, causal_conv1d_varlen_states_ref(x, cu, S), f"S={S}")
         assert_bitwise(got, oracle.varlen_states(x, cu, S), f"S={S} (oracle)")
+
+
+@pytest.mark.parametrize("pool", [False, True])
+@pytest.mark.parametrize("dtype,W", [("bf16", 2), ("bf16", 4), ("bf16", 9), ("fp16", 5), ("fp32", 2), ("fp32", 5)])
+def test_circular_serving_state_len_vs_oracle(dtype, W, pool):
+    """Circular decode with the serving state_len (8 for 16-bit types, 4 for
+    fp32), full write-head range incl. negative and wrapped values."""
+    dt = DTYPES[dtype]
+    S = 16 // torch.tensor([], dtype=dt).element_size()
+    B, D = 7, 1024
+    rows = 2 * B if pool else B
+    x = seeded((B, D), dt, W)
+    w = seeded((D, W), dt, W + 1, "uniform")
+    b = seeded((D,), dt, W + 2, "uniform")
+    state = seeded((rows, D, S), dt, W + 3)
+    cache = torch.tensor([0, 1, S - 1, S, 1023, -1, -S - 3], dtype=torch.int32)
+    idx = None
+    if pool:
+        idx = torch.randperm(rows, generator=torch.Generator().manual_seed(W))[:B].to(torch.int32)
+        idx[2] = -1
+    st_g = state.to(DEV)
+    out = causal_conv1d_update(x.to(DEV), st_g, w.to(DEV), b.to(DEV), activation="silu", cache_seqlens=cache.to(DEV),
+                               conv_state_indices=idx.to(DEV) if idx is not None else None)
+    st_o = state.clone()
+    o = oracle.update(x, st_o, w, b, silu=True, cache_seqlens=cache, conv_state_indices=idx)
+    assert_close(out.cpu(), o, dt, "out")
+    assert_bitwise(st_g.cpu(), st_o, "conv_state")
