@@ -190,27 +190,60 @@ __global__ void __launch_bounds__(kThreadsTma, CC1D_FWD_MIN_BLOCKS) fwd_chan_tma
       int sreg = 0;
       if (HAS_SEQ) sreg = (t + lane < t1 && lane < TR) ? seq[b * a.ss_b + (t + lane) * a.ss_l] : kNoSeq;
       const int nr = (int)min((i64)TR, t1 - t);
+      // With seq_idx, a tile whose rows and W-1 halo all carry the same
+      // non-negative id (no sequence boundary, no padding) needs no gating.
+      bool gate = HAS_SEQ;
+      if (HAS_SEQ) {
+        const int s0 = sw[0];
+        bool same = s0 >= 0;
 #pragma unroll
-      for (int rr = 0; rr < TR; ++rr) {
-        if (rr >= nr) break;
-        const float2 xv = P::unpack(tile[rr * ROW_WORDS]);
-        const int sid = HAS_SEQ ? __shfl_sync(kFull, sreg, rr) : 0;
-        float2 acc = bv;
+        for (int j = 1; j < H; ++j) same = same && sw[j] == s0;
+        same = __all_sync(kFull, same && (lane >= nr || sreg == s0));
+        if (same) {
+          gate = false;
 #pragma unroll
-        for (int j = 0; j < H; ++j)
-          if (!HAS_SEQ || sw[j] == sid) acc = fma2(wv[j], xw[j], acc);
-        acc = fma2(wv[H], xv, acc);
-        if (SILU) acc = silu2(acc);
-        if (HAS_SEQ && sid < 0) acc = f2(0.f, 0.f);
-        if (valid) *reinterpret_cast<PW*>(orow) = P::pack(acc);
-        orow += a.os_l;
-#pragma unroll
-        for (int j = 0; j < H - 1; ++j) {
-          xw[j] = xw[j + 1];
-          sw[j] = sw[j + 1];
+          for (int j = 0; j < H; ++j) sw[j] = s0;
         }
-        xw[H - 1] = xv;
-        sw[H - 1] = sid;
+      }
+      if (gate) {
+#pragma unroll
+        for (int rr = 0; rr < TR; ++rr) {
+          if (rr >= nr) break;
+          const float2 xv = P::unpack(tile[rr * ROW_WORDS]);
+          const int sid = __shfl_sync(kFull, sreg, rr);
+          float2 acc = bv;
+#pragma unroll
+          for (int j = 0; j < H; ++j)
+            if (sw[j] == sid) acc = fma2(wv[j], xw[j], acc);
+          acc = fma2(wv[H], xv, acc);
+          if (SILU) acc = silu2(acc);
+          if (sid < 0) acc = f2(0.f, 0.f);
+          if (valid) *reinterpret_cast<PW*>(orow) = P::pack(acc);
+          orow += a.os_l;
+#pragma unroll
+          for (int j = 0; j < H - 1; ++j) {
+            xw[j] = xw[j + 1];
+            sw[j] = sw[j + 1];
+          }
+          xw[H - 1] = xv;
+          sw[H - 1] = sid;
+        }
+      } else {
+#pragma unroll
+        for (int rr = 0; rr < TR; ++rr) {
+          if (rr >= nr) break;
+          const float2 xv = P::unpack(tile[rr * ROW_WORDS]);
+          float2 acc = bv;
+#pragma unroll
+          for (int j = 0; j < H; ++j) acc = fma2(wv[j], xw[j], acc);
+          acc = fma2(wv[H], xv, acc);
+          if (SILU) acc = silu2(acc);
+          if (valid) *reinterpret_cast<PW*>(orow) = P::pack(acc);
+          orow += a.os_l;
+#pragma unroll
+          for (int j = 0; j < H - 1; ++j) xw[j] = xw[j + 1];
+          xw[H - 1] = xv;
+        }
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(&empty[s]);
@@ -230,7 +263,7 @@ __global__ void __launch_bounds__(kThreadsTma, CC1D_FWD_MIN_BLOCKS) fwd_chan_tma
 // Backward
 // ---------------------------------------------------------------------------
 
-template <typename T, int W, bool HAS_SEQ, bool SILU>
+template <typename T, int W>
 struct BwdState {
   float2 wv[W];
   float2 bv;
@@ -246,7 +279,7 @@ struct BwdState {
 // dinitial_states) of position t-H.  CHECK=false is the interior path
 // (own and emit known true, no states involved).
 template <typename T, int W, bool HAS_SEQ, bool SILU, bool CHECK>
-__device__ __forceinline__ void bwd_step(BwdState<T, W, HAS_SEQ, SILU>& st, float2 xv, float2 gv, int sid, bool own,
+__device__ __forceinline__ void bwd_step(BwdState<T, W>& st, float2 xv, float2 gv, int sid, bool own,
                                          bool emit, T* dxrow, const BwdArgs& a, i64 b, i64 c, i64 p, bool valid) {
   constexpr int H = W - 1;
   typedef Pair<T> P;
@@ -367,7 +400,7 @@ __global__ void __launch_bounds__(kThreadsTma, CC1D_BWD_MIN_BLOCKS) bwd_chan_tma
   const int* __restrict__ seq = a.seq;
   T* __restrict__ dx = static_cast<T*>(a.dx);
 
-  BwdState<T, W, HAS_SEQ, SILU> st;
+  BwdState<T, W> st;
 #pragma unroll
   for (int k = 0; k < W; ++k) {
     st.wv[k] = valid ? load_pair_strided(wt + c * a.ws_c + k * a.ws_k, a.ws_c) : f2(0.f, 0.f);
@@ -407,14 +440,31 @@ __global__ void __launch_bounds__(kThreadsTma, CC1D_BWD_MIN_BLOCKS) bwd_chan_tma
       int sreg = 0;
       if (HAS_SEQ) sreg = (t + lane < tl && lane < TR) ? seq[b * a.ss_b + (t + lane) * a.ss_l] : kNoSeq;
       const int nr = (int)min((i64)TR, tl - t);
-      if (nr == TR && t >= t0 + H && t + TR <= t1) {
+      // With seq_idx, a tile whose rows and W-1 halo all carry the same
+      // non-negative id needs no gating (dx of its rows reads dpre of the
+      // next W-1 rows, which are in this tile or gated by the later tiles'
+      // own checks through the dpre window's ids).
+      bool gate = HAS_SEQ;
+      if (HAS_SEQ) {
+        const int s0 = st.sw[0];
+        bool same = s0 >= 0;
+#pragma unroll
+        for (int j = 1; j < H; ++j) same = same && st.sw[j] == s0;
+        same = __all_sync(kFull, same && (lane >= nr || sreg == s0));
+        if (same) gate = false;
+      }
+      if (!gate && nr == TR && t >= t0 + H && t + TR <= t1) {
         // Interior tile: every step owns its row and emits a dx row.
+        const int s0 = HAS_SEQ ? st.sw[0] : 0;
 #pragma unroll
         for (int rr = 0; rr < TR; ++rr) {
-          const int sid = HAS_SEQ ? __shfl_sync(kFull, sreg, rr) : 0;
-          bwd_step<T, W, HAS_SEQ, SILU, false>(st, P::unpack(tx[rr * ROW_WORDS]), P::unpack(tg[rr * ROW_WORDS]),
-                                                sid, true, true, dxrow, a, b, c, 0, valid);
+          bwd_step<T, W, false, SILU, false>(st, P::unpack(tx[rr * ROW_WORDS]), P::unpack(tg[rr * ROW_WORDS]), 0,
+                                             true, true, dxrow, a, b, c, 0, valid);
           dxrow += a.dxs_l;
+        }
+        if (HAS_SEQ) {
+#pragma unroll
+          for (int j = 0; j < H; ++j) st.sw[j] = s0;
         }
       } else {
 #pragma unroll

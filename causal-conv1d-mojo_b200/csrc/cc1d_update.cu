@@ -199,89 +199,11 @@ __global__ void __launch_bounds__(128) update_vec_kernel(const UpdateArgs a) {
   }
 }
 
-// Single-token circular-buffer decode when each channel's state row is
-// exactly 16 bytes (state_len 8 for 16-bit types, 4 for fp32) and rows are
-// contiguous.  Same channel mapping as update_circ_kernel below (lane l owns
-// channels l + 32*v, so a warp-wide access covers 32 consecutive channels),
-// but each state row moves as one 16-byte vector: a warp reads and writes
-// 512 contiguous bytes per instruction.  The write head cs is the same for
-// the whole batch row, so the window positions (cs-(W-1)+j) mod S are
-// uniform and elements are picked by selects (no dynamic register
-// indexing); the new token is merged into the row and the row is written
-// back whole.
-template <typename T, int W>
-__global__ void __launch_bounds__(128) update_circ_vec_kernel(const UpdateArgs a) {
-  constexpr int H = W - 1;
-  constexpr int V = 8;
-  constexpr int CHUNK = 128 * V;  // channels per block (4 warps x 256)
-  constexpr int E16 = 16 / sizeof(T);  // = state_len
-  typedef Pack<T, E16> P16;
-  const i64 chunks = ceil_div(a.D, (i64)CHUNK);
-  const i64 b = blockIdx.x / chunks;
-  const i64 cbase = (blockIdx.x - b * chunks) * CHUNK + (threadIdx.x >> 5) * 256 + (threadIdx.x & 31);
-  const T* __restrict__ x = static_cast<const T*>(a.x);
-  const T* __restrict__ wt = static_cast<const T*>(a.w);
-  const T* __restrict__ bias = static_cast<const T*>(a.bias);
-  T* __restrict__ out = static_cast<T*>(a.out);
-  i64 row = b;
-  if (a.idx != nullptr) {
-    const int r = a.idx[b];
-    if (r < 0 || r >= a.state_rows) {
-#pragma unroll
-      for (int v = 0; v < V; ++v) {
-        const i64 c = cbase + 32 * v;
-        if (c < a.D) out[b * a.os_b + c * a.os_c] = Cvt<T>::to(0.f);
-      }
-      return;
-    }
-    row = r;
-  }
-  T* __restrict__ st = static_cast<T*>(a.state) + row * a.ss_b;
-  P16 rows[V];
-  T xv[V];
-  float acc[V];
-#pragma unroll
-  for (int v = 0; v < V; ++v) {
-    const i64 c = cbase + 32 * v;
-    if (c < a.D) {
-      rows[v] = ld_pack<T, E16>(st + c * E16);
-      xv[v] = x[b * a.xs_b + c * a.xs_c];
-      acc[v] = bias ? Cvt<T>::f(bias[c * a.bs]) : 0.f;
-    }
-  }
-  int cs = (int)((i64)a.cache_seqlens[b] % E16);
-  if (cs < 0) cs += E16;
-  int pos[H];
-#pragma unroll
-  for (int j = 0; j < H; ++j) pos[j] = (cs - H + j + 2 * E16 * H) % E16;
-#pragma unroll
-  for (int v = 0; v < V; ++v) {
-    const i64 c = cbase + 32 * v;
-    if (c < a.D) {
-#pragma unroll
-      for (int k = 0; k < H; ++k) {
-        T h = rows[v].v[0];
-#pragma unroll
-        for (int e = 1; e < E16; ++e) h = (pos[k] == e) ? rows[v].v[e] : h;
-        acc[v] = fmaf(Cvt<T>::f(wt[c * a.ws_c + k * a.ws_k]), Cvt<T>::f(h), acc[v]);
-      }
-      acc[v] = fmaf(Cvt<T>::f(wt[c * a.ws_c + H * a.ws_k]), Cvt<T>::f(xv[v]), acc[v]);
-    }
-  }
-#pragma unroll
-  for (int v = 0; v < V; ++v) {
-    const i64 c = cbase + 32 * v;
-    if (c < a.D) {
-      float o = acc[v];
-      if (a.silu) o = silu_f(o);
-      out[b * a.os_b + c * a.os_c] = Cvt<T>::to(o);
-#pragma unroll
-      for (int e = 0; e < E16; ++e) rows[v].v[e] = (e == cs) ? xv[v] : rows[v].v[e];
-      st_pack<T, E16>(st + c * E16, rows[v]);
-    }
-  }
-}
-
+// Single-token circular-buffer decode (any strides, any state_len).  A warp
+// owns 256 channels of one batch row, lane l the channels l + 32*v (v < 8), so
+// every warp-wide access touches 32 consecutive channel rows.  All loads of a
+// thread's 8 channels are issued before any store (no read-after-write
+// ordering between channels); two dependent memory round trips per block.
 template <typename T, int W>
 __global__ void __launch_bounds__(128) update_circ_kernel(const UpdateArgs a) {
   constexpr int H = W - 1;
@@ -397,14 +319,6 @@ bool vec_path_ok(const UpdateArgs& a) {
          (a.bias == nullptr || (a.bs == 1 && aligned16(a.bias)));
 }
 
-// Conditions of update_circ_vec_kernel (see its comment).
-template <typename T, int W>
-bool circ_vec_path_ok(const UpdateArgs& a) {
-  const i64 e = 16 / (i64)sizeof(T);
-  return a.cache_seqlens != nullptr && a.L == 1 && a.S == e && a.ss_l == 1 && a.ss_c == a.S && aligned16(a.state) &&
-         (a.ss_b % e == 0);
-}
-
 struct LaunchUpdate {
   const UpdateArgs& a;
   cudaStream_t stream;
@@ -415,12 +329,6 @@ struct LaunchUpdate {
       const i64 blocks = ceil_div(a.D / 8, (i64)threads) * a.B;
       if (blocks > 0x7fffffffLL) return cudaErrorInvalidConfiguration;
       update_vec_kernel<T, W><<<(unsigned)blocks, threads, 0, stream>>>(a);
-      return cudaGetLastError();
-    }
-    if (circ_vec_path_ok<T, W>(a)) {
-      const i64 blocks = ceil_div(a.D, (i64)threads * 8) * a.B;
-      if (blocks > 0x7fffffffLL) return cudaErrorInvalidConfiguration;
-      update_circ_vec_kernel<T, W><<<(unsigned)blocks, threads, 0, stream>>>(a);
       return cudaGetLastError();
     }
     if (a.cache_seqlens != nullptr && a.L == 1) {
