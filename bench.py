@@ -428,14 +428,24 @@ def time_kernels(peak):
 # CPU path (oracle port): baseline leg and reference arm
 # --------------------------------------------------------------------------
 
+def host_cores():
+    """Host threads available to this process (torchrun sets
+    OMP_NUM_THREADS=1 for its workers, so OpenMP's default is not used)."""
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:
+        return os.cpu_count() or 1
+
+
 def cpu_sample_step(state):
     """One sample step of the reference CPU algorithm: forward + backward of
-    batch row 0 of C2 (1, 5376, 2048), float accumulation, all threads."""
+    batch row 0 of C2 (1, 5376, 2048), float accumulation, all host threads."""
     import oracle
 
     x, w, b, init, dout = state
-    oracle.fwd(x, w, b, None, init, silu=True, return_final_states=True, acc64=False)
-    oracle.bwd(x, w, dout, b, None, init, None, silu=True, acc64=False)
+    n = host_cores()
+    oracle.fwd(x, w, b, None, init, silu=True, return_final_states=True, acc64=False, nthreads=n)
+    oracle.bwd(x, w, dout, b, None, init, None, silu=True, acc64=False, nthreads=n)
 
 
 def cpu_setup():
@@ -448,7 +458,7 @@ def cpu_setup():
     b = (torch.rand(D, generator=g) - 0.5).to(DT)
     init = torch.randn(1, D, W - 1, generator=g).to(DT)
     dout = torch.randn(1, L, D, generator=g).to(DT).transpose(1, 2)
-    return (x, w, b, init, dout), oracle.max_threads()
+    return (x, w, b, init, dout), host_cores()
 
 
 def cpu_baseline(budget_s=10.0):
