@@ -212,9 +212,8 @@ def graph_ms(g, reps, per_graph):
     return a.elapsed_time(c) / (reps * per_graph)
 
 
-def time_c2(args, world, rank):
+def time_c2(args, world, rank, reducer):
     from causal_conv1d_b200 import _ops
-    from causal_conv1d_b200.parallel import allreduce_weight_grads, split_dwdb
 
     x, w, b, init, dout = make_c2(1234 + rank, "cuda")
     out = torch.empty_like(x)
@@ -230,19 +229,16 @@ def time_c2(args, world, rank):
         _ops.fwd(x, w, b, None, init, out, True, fs)
 
     def bwd(_=0):
-        if world > 1:
-            _ops.bwd(x, w, b, dout, None, init, None, dx, dwdb, dinit, None, None, True)
+        if reducer is not None:
+            # dweight/dbias summed over the ranks inside the reduction kernel
+            # (NVLink peer memory), written straight into dw / db.
+            _ops.bwd_peer(x, w, b, dout, init, None, dx, dwdb, dinit, dw, db, True, *reducer.args())
         else:
             _ops.bwd(x, w, b, dout, None, init, None, dx, dwdb, dinit, dw, db, True)
 
     def step(_=0):
         fwd()
         bwd()
-        if world > 1:
-            allreduce_weight_grads(dwdb)
-            gw, gb = split_dwdb(dwdb, D, W)
-            dw.copy_(gw)
-            db.copy_(gb)
 
     with Clocks(torch.cuda.current_device()) as clk:
         # The sampler starts before the warm-up so that it is already
@@ -276,7 +272,7 @@ def time_c2(args, world, rank):
     return dict(ms_per_step=total_ms / K, fwd_ms=fwd_ms, bwd_ms=bwd_ms, clocks=clk.summary())
 
 
-def time_e2e(args, world, rank):
+def time_e2e(args, world, rank, reducer):
     """Public API, host buffers in and out, every step."""
     from causal_conv1d_b200 import causal_conv1d_fn
     from causal_conv1d_b200.parallel import causal_conv1d_fn_batch_sharded
@@ -299,7 +295,7 @@ def time_e2e(args, world, rank):
         dout = host["dout"].to("cuda", non_blocking=True).transpose(1, 2)
         if world > 1:
             out, fs = causal_conv1d_fn_batch_sharded(x, w, b, initial_states=init, return_final_states=True,
-                                                      activation="silu")
+                                                      activation="silu", reducer=reducer)
         else:
             out, fs = causal_conv1d_fn(x, w, b, initial_states=init, return_final_states=True, activation="silu")
         torch.autograd.backward([out], [dout])
@@ -621,8 +617,13 @@ def main():
     peak, peak_kind = peaks()
     fwd_bytes, bwd_bytes = c2_bytes()
 
-    r = time_c2(args, world, rank)
-    e2e = None if args.skip_e2e else time_e2e(args, world, rank)
+    reducer = None
+    if world > 1:
+        from causal_conv1d_b200.parallel import PeerReducer
+
+        reducer = PeerReducer(D, W, torch.device("cuda", local))
+    r = time_c2(args, world, rank, reducer)
+    e2e = None if args.skip_e2e else time_e2e(args, world, rank, reducer)
     kernels = None
     if rank == 0 and not args.skip_kernels:
         kernels = time_kernels(peak)
@@ -639,7 +640,9 @@ def main():
         ktab = {
             "fwd_c2": dict(ms=r["fwd_ms"], gbs=fwd_gbs, frac=fwd_gbs / peak, algorithmic_bytes=fwd_bytes),
             "bwd_c2": dict(ms=r["bwd_ms"], gbs=bwd_gbs, frac=bwd_gbs / peak, algorithmic_bytes=bwd_bytes,
-                           note="bwd kernel + dweight/dbias finalize kernel"),
+                           note="bwd kernel + dweight/dbias finalize kernel" + (
+                               " (fused with the cross-rank sum, so it includes waiting for peers)"
+                               if world > 1 else "")),
         }
         if kernels:
             ktab.update(kernels)
@@ -660,8 +663,9 @@ def main():
                 "workload": "C2 Mamba-2 2.7B prefill: causal_conv1d_fn fwd+bwd, bf16, x (8, 5376, 2048) "
                             "channel-last, width 4, bias, SiLU, initial_states, return_final_states",
                 "global_batch": world * B, "seq_len": L, "dim": D, "width": W,
-                "parallelism": f"batch-sharded x{world}" + (", NCCL all-reduce of fp32 dweight|dbias"
-                                                            if world > 1 else ""),
+                "parallelism": f"batch-sharded x{world}" + (
+                    ", dweight|dbias summed over ranks inside the reduction kernel over NVLink peer memory"
+                    if world > 1 else ""),
                 "l2": "inputs larger than L2 (x and grad_out are 176 MB each; L2 is 126 MB)",
             },
             "roofline": {
@@ -681,6 +685,7 @@ def main():
             line["cpu_baseline"] = cpu
         print(json.dumps(line), flush=True)
     if world > 1:
+        reducer.close()
         dist.barrier()
         dist.destroy_process_group()
     return 0

@@ -205,6 +205,59 @@ bwd = torch.library.custom_op(
 bwd.register_fake(_bwd_fake)
 
 
+def _bwd_peer_impl(
+    x: torch.Tensor,
+    weight: torch.Tensor,
+    bias: torch.Tensor | None,
+    dout: torch.Tensor,
+    initial_states: torch.Tensor | None,
+    dfinal_states: torch.Tensor | None,
+    dx: torch.Tensor,
+    dwdb_acc: torch.Tensor,
+    dinitial_states: torch.Tensor | None,
+    dweight_out: torch.Tensor | None,
+    dbias_out: torch.Tensor | None,
+    apply_silu: bool,
+    exchange_ptrs: torch.Tensor,
+    flag_ptrs: torch.Tensor,
+    epochs: torch.Tensor,
+    rank: int,
+    world: int,
+) -> None:
+    """Backward of a batch shard with dweight/dbias summed over `world` ranks
+    in the same kernel (cc1d_bwd_peer_reduce).  exchange_ptrs / flag_ptrs:
+    int64 device tensors of the ranks' peer-mapped buffer addresses."""
+    _require_cuda(x, "causal_conv1d_fn backward (peer reduce)")
+    lib = _lib.load()
+    p = _bwd_params(x, weight, bias, dout, None, initial_states, dfinal_states, dx, dwdb_acc, dinitial_states,
+                    dweight_out, dbias_out, apply_silu)
+    q = _lib.PeerReduceParams()
+    q.rank, q.world = rank, world
+    q.exchange, q.flags, q.epochs = exchange_ptrs.data_ptr(), flag_ptrs.data_ptr(), epochs.data_ptr()
+    with _on_device(x.device):
+        nbytes = bwd_workspace_bytes(p)
+        ws = None
+        if nbytes > 0:
+            ws = torch.empty(nbytes, dtype=torch.uint8, device=x.device)
+            p.workspace = ws.data_ptr()
+            p.workspace_bytes = nbytes
+        _lib.check(lib.cc1d_bwd_peer_reduce(ctypes.byref(p), ctypes.byref(q), _stream(x.device)),
+                   "cc1d_bwd_peer_reduce")
+        del ws
+
+
+def _bwd_peer_fake(x, weight, bias, dout, initial_states, dfinal_states, dx, dwdb_acc, dinitial_states,
+                   dweight_out, dbias_out, apply_silu, exchange_ptrs, flag_ptrs, epochs, rank, world) -> None:
+    return None
+
+
+bwd_peer = torch.library.custom_op(
+    "causal_conv1d_b200::bwd_peer",
+    mutates_args=("dx", "dwdb_acc", "dinitial_states", "dweight_out", "dbias_out", "epochs"),
+)(_bwd_peer_impl)
+bwd_peer.register_fake(_bwd_peer_fake)
+
+
 def _update_impl(
     x: torch.Tensor,
     conv_state: torch.Tensor,

@@ -12,8 +12,18 @@ with no data exchange:
   Mamba shapes that buffer is ~100-170 KB, so the collective is
   latency-bound.
 
-The all-reduce goes through ``torch.distributed`` (NCCL on GPUs; the host
-logic is exercised with gloo on CPU).
+Two implementations of that all-reduce:
+
+* ``PeerReducer`` (GPUs on one node): the backward's final reduction kernel
+  also performs the cross-GPU sum, reading the peers' partial sums over
+  NVLink from IPC-mapped buffers (cc1d_bwd_peer_reduce).  One launch replaces
+  finalize -> all-reduce -> dtype casts, and every rank gets bitwise
+  identical gradients, summed in rank order.
+* ``allreduce_weight_grads``: one ``torch.distributed`` all-reduce of the
+  fp32 buffer (NCCL on GPUs; the host logic is exercised with gloo on CPU).
+
+The reference (gabrieldemarmiesse/causal-conv1d-mojo) has no multi-GPU code;
+this module is the data-parallel use of its causal_conv1d_fn.
 """
 
 from __future__ import annotations
@@ -21,7 +31,7 @@ from __future__ import annotations
 import torch
 import torch.distributed as dist
 
-from . import _ops
+from . import _lib, _ops
 from ._fn import _like_layout
 
 
@@ -57,16 +67,124 @@ def allreduce_weight_grads(dwdb: torch.Tensor, group=None) -> torch.Tensor:
     return dwdb
 
 
+def _rt_check(res, what: str):
+    err = res[0] if isinstance(res, tuple) else res
+    if int(err) != 0:
+        raise RuntimeError(f"{what} failed: {err}")
+    return res[1] if isinstance(res, tuple) and len(res) == 2 else None
+
+
+class PeerReducer:
+    """Peer-mapped buffers for the fused backward reduction over `group`
+    (one process per GPU, all GPUs of one node).
+
+    Each rank cudaMallocs an exchange buffer (2*dim*(width+1) fp32: one half
+    per call parity) and a flag array (world * cc1d_peer_blocks(dim, width)
+    uint32), exports them as CUDA IPC handles, gathers the peers' handles
+    over `group` and maps them.  Plain peer memory -- no multicast object.
+    Construction and ``close()`` are collective over `group`; every rank must
+    then issue the same sequence of backward calls with the same dim/width.
+    The per-block call counters live on the device, so those calls may be
+    captured in a CUDA graph and replayed.
+    """
+
+    def __init__(self, dim: int, width: int, device: torch.device | str | int | None = None, group=None):
+        from cuda.bindings import runtime as rt
+
+        if not (dist.is_available() and dist.is_initialized()):
+            raise RuntimeError("PeerReducer needs an initialised torch.distributed process group")
+        self._rt = rt
+        self.group = group
+        self.rank = dist.get_rank(group)
+        self.world = dist.get_world_size(group)
+        if self.world > 32:
+            raise ValueError("PeerReducer supports at most 32 ranks")
+        dev = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
+        if dev.type != "cuda":
+            raise ValueError("PeerReducer needs a CUDA device")
+        if dev.index is None:
+            dev = torch.device("cuda", torch.cuda.current_device())
+        self.device, self.dim, self.width = dev, dim, width
+        self.nblocks = int(_lib.load().cc1d_peer_blocks(dim, width))
+        ex_bytes = max(2 * dim * (width + 1) * 4, 16)
+        fl_bytes = max(self.world * self.nblocks * 4, 16)
+        _rt_check(rt.cudaSetDevice(dev.index), "cudaSetDevice")
+        self._own = [_rt_check(rt.cudaMalloc(ex_bytes), "cudaMalloc"), _rt_check(rt.cudaMalloc(fl_bytes), "cudaMalloc")]
+        _rt_check(rt.cudaMemset(self._own[0], 0, ex_bytes), "cudaMemset")
+        _rt_check(rt.cudaMemset(self._own[1], 0, fl_bytes), "cudaMemset")
+        _rt_check(rt.cudaDeviceSynchronize(), "cudaDeviceSynchronize")
+        handles = [bytes(_rt_check(rt.cudaIpcGetMemHandle(p), "cudaIpcGetMemHandle").reserved) for p in self._own]
+        uuid = str(torch.cuda.get_device_properties(dev).uuid)
+        gathered: list = [None] * self.world
+        dist.all_gather_object(gathered, (uuid, handles), group=group)
+        if len({g[0] for g in gathered}) != self.world:
+            # The reduction kernels of different ranks wait for one another;
+            # two of them queued on one GPU are not guaranteed to run together.
+            for p in self._own:
+                rt.cudaFree(p)
+            self._own = None
+            raise ValueError("PeerReducer needs one GPU per rank (two ranks share a device)")
+        gathered = [g[1] for g in gathered]
+        self._mapped = []
+        ptrs = [[0] * self.world, [0] * self.world]
+        for r in range(self.world):
+            for j in range(2):
+                if r == self.rank:
+                    ptrs[j][r] = int(self._own[j])
+                    continue
+                h = rt.cudaIpcMemHandle_t()
+                h.reserved = gathered[r][j]
+                mp = _rt_check(rt.cudaIpcOpenMemHandle(h, rt.cudaIpcMemLazyEnablePeerAccess), "cudaIpcOpenMemHandle")
+                self._mapped.append(mp)
+                ptrs[j][r] = int(mp)
+        self.exchange_ptrs = torch.tensor(ptrs[0], dtype=torch.int64, device=dev)
+        self.flag_ptrs = torch.tensor(ptrs[1], dtype=torch.int64, device=dev)
+        self.epochs = torch.zeros(max(self.nblocks, 1), dtype=torch.int32, device=dev)
+        torch.cuda.synchronize(dev)
+        dist.barrier(group=group)
+
+    def args(self) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor, int, int]:
+        """(exchange_ptrs, flag_ptrs, epochs, rank, world) for ``_ops.bwd_peer``."""
+        if self._own is None:
+            raise RuntimeError("PeerReducer is closed")
+        return self.exchange_ptrs, self.flag_ptrs, self.epochs, self.rank, self.world
+
+    def close(self) -> None:
+        """Collective: unmap the peers' buffers, then free this rank's."""
+        if self._own is None:
+            return
+        rt = self._rt
+        torch.cuda.synchronize(self.device)
+        dist.barrier(group=self.group)  # no rank still reads or signals
+        _rt_check(rt.cudaSetDevice(self.device.index), "cudaSetDevice")
+        for mp in self._mapped:
+            _rt_check(rt.cudaIpcCloseMemHandle(mp), "cudaIpcCloseMemHandle")
+        self._mapped = []
+        dist.barrier(group=self.group)  # every peer has unmapped this rank's buffers
+        for p in self._own:
+            _rt_check(rt.cudaFree(p), "cudaFree")
+        self._own = None
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()
+        return False
+
+
 class _BatchShardedFn(torch.autograd.Function):
-    """causal_conv1d_fn over a batch shard; backward all-reduces dW/db."""
+    """causal_conv1d_fn over a batch shard; backward sums dW/db over ranks
+    (fused peer reduction when a PeerReducer is given, else all-reduce)."""
 
     @staticmethod
-    def forward(ctx, x, weight, bias, initial_states, apply_silu, final_states_out, group):
+    def forward(ctx, x, weight, bias, initial_states, apply_silu, final_states_out, group, reducer):
         out = torch.empty_like(x)
         _ops.fwd(x, weight, bias, None, initial_states, out, apply_silu, final_states_out)
         ctx.save_for_backward(x, weight, bias, initial_states)
         ctx.apply_silu = apply_silu
         ctx.group = group
+        ctx.reducer = reducer
         ctx.return_final_states = final_states_out is not None
         if final_states_out is not None:
             return out, final_states_out
@@ -82,10 +200,19 @@ class _BatchShardedFn(torch.autograd.Function):
         dx = torch.empty_like(x)
         dwdb = torch.empty(D * (W + 1), dtype=torch.float32, device=x.device)
         dinit = torch.empty_like(initial_states) if initial_states is not None else None
+        if ctx.reducer is not None:
+            if (ctx.reducer.dim, ctx.reducer.width) != (D, W):
+                raise ValueError("PeerReducer was built for another (dim, width)")
+            dw = torch.empty(D, W, dtype=weight.dtype, device=x.device)
+            db = torch.empty(D, dtype=bias.dtype, device=x.device) if bias is not None else None
+            _ops.bwd_peer(x, weight, bias, dout, initial_states, dfinal, dx, dwdb, dinit, dw, db, ctx.apply_silu,
+                          *ctx.reducer.args())
+            return dx, dw, db, dinit, None, None, None, None
         _ops.bwd(x, weight, bias, dout, None, initial_states, dfinal, dx, dwdb, dinit, None, None, ctx.apply_silu)
         allreduce_weight_grads(dwdb, ctx.group)
         dw, db = split_dwdb(dwdb, D, W)
-        return (dx, dw.to(weight.dtype), db.to(bias.dtype) if bias is not None else None, dinit, None, None, None)
+        return (dx, dw.to(weight.dtype), db.to(bias.dtype) if bias is not None else None, dinit, None, None, None,
+                None)
 
 
 def causal_conv1d_fn_batch_sharded(
@@ -96,13 +223,16 @@ def causal_conv1d_fn_batch_sharded(
     return_final_states: bool = False,
     activation: str | None = None,
     group=None,
+    reducer: PeerReducer | None = None,
 ):
     """causal_conv1d_fn on this rank's batch shard `x` with replicated
     weight/bias: weight.grad / bias.grad come out summed over all ranks of
-    `group` (the data-parallel gradient), x.grad stays local."""
+    `group` (the data-parallel gradient), x.grad stays local.  With a
+    `reducer` the sum is fused into the backward kernel over NVLink peer
+    memory; otherwise one all-reduce over `group`."""
     if activation not in (None, "silu", "swish"):
         raise NotImplementedError("only activation in {None, 'silu', 'swish'} is supported")
     batch, dim, _ = x.shape
     width = weight.shape[1]
     fs = torch.empty(batch, dim, width - 1, dtype=x.dtype, device=x.device) if return_final_states else None
-    return _BatchShardedFn.apply(x, weight, bias, initial_states, activation in ("silu", "swish"), fs, group)
+    return _BatchShardedFn.apply(x, weight, bias, initial_states, activation in ("silu", "swish"), fs, group, reducer)

@@ -24,8 +24,43 @@ int fail(int code, const char* fmt, ...) {
   return code;
 }
 
+thread_local char g_detail[160] = {0};
+
 int cuda_fail(cudaError_t e, const char* what) {
-  return fail(CC1D_ERR_CUDA, "%s: %s (%s)", what, cudaGetErrorString(e), cudaGetErrorName(e));
+  int dev = -1;
+  (void)cudaGetDevice(&dev);
+  (void)cudaGetLastError();  // the error is reported here, not by the next call
+  fail(CC1D_ERR_CUDA, "%s: %s (%s) on device %d%s%s", what, cudaGetErrorString(e), cudaGetErrorName(e), dev,
+       g_detail[0] ? ": " : "", g_detail);
+  g_detail[0] = 0;
+  return CC1D_ERR_CUDA;
+}
+
+// Device the calling thread was last bound to by bind_device.
+thread_local int t_bound_device = -1;
+
+// Makes the device that holds `ptr` current on the calling thread, with its
+// primary context bound (the driver-level tensor-map encoder needs one).
+// The caller's framework keeps its own runtime state and may never have
+// bound a context on this thread (e.g. an autograd worker thread of device
+// 0), so the device is taken from the data, not inherited.  Host or
+// unregistered pointers leave the current device alone.
+int bind_device(const void* ptr, const char* what) {
+  if (ptr == nullptr) return CC1D_OK;
+  cudaPointerAttributes at;
+  cudaError_t e = cudaPointerGetAttributes(&at, ptr);
+  if (e != cudaSuccess) {
+    (void)cudaGetLastError();
+    return CC1D_OK;
+  }
+  if (at.type != cudaMemoryTypeDevice || at.device < 0) return CC1D_OK;
+  int cur = -1;
+  e = cudaGetDevice(&cur);
+  if (e == cudaSuccess && (cur != at.device || t_bound_device != at.device)) {
+    e = cudaSetDevice(at.device);  // initialises and binds the primary context
+    if (e == cudaSuccess) t_bound_device = at.device;
+  }
+  return e == cudaSuccess ? CC1D_OK : cuda_fail(e, what);
 }
 
 int ok() {
@@ -58,6 +93,13 @@ int report_error(int code, const char* fmt, ...) {
 }
 
 int report_cuda_error(cudaError_t e, const char* what) { return cuda_fail(e, what); }
+
+void set_error_detail(const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_detail, sizeof(g_detail), fmt, ap);
+  va_end(ap);
+}
 
 cudaError_t device_info(DeviceInfo* out) {
   int dev = 0;
@@ -172,6 +214,7 @@ int cc1d_fwd(const cc1d_fwd_params* p, void* stream) {
   if (rc) return rc;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (p->batch * p->dim == 0) return ok();
+  if ((rc = bind_device(p->out, "cc1d_fwd")) != CC1D_OK) return rc;
   if (p->seqlen == 0) {
     cudaError_t e = launch_fwd_empty_seq(p->dtype, p->width, a, s);
     return e == cudaSuccess ? ok() : cuda_fail(e, "cc1d_fwd (empty sequence)");
@@ -199,6 +242,7 @@ int cc1d_bwd_workspace_size(const cc1d_bwd_params* p, size_t* bytes) {
   int rc = bwd_args(p, &a);
   if (rc) return rc;
   if (p->batch * p->dim * p->seqlen == 0) return ok();
+  if ((rc = bind_device(p->dwdb_acc, "cc1d_bwd_workspace_size")) != CC1D_OK) return rc;
   Plan plan;
   std::memset(&plan, 0, sizeof(plan));
   cudaError_t e = plan_bwd_any(p->dtype, p->width, a, &plan);
@@ -207,12 +251,26 @@ int cc1d_bwd_workspace_size(const cc1d_bwd_params* p, size_t* bytes) {
   return ok();
 }
 
-int cc1d_bwd(const cc1d_bwd_params* p, void* stream) {
+}  // extern "C"
+
+namespace {
+
+// cc1d_bwd, optionally with the dweight/dbias reduction fused with a
+// cross-GPU all-reduce (peer != nullptr).
+int bwd_impl(const cc1d_bwd_params* p, const cc1d_peer_reduce* peer, void* stream) {
   BwdArgs a;
   int rc = bwd_args(p, &a);
   if (rc) return rc;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (peer != nullptr) {
+    if (peer->world < 1 || peer->rank < 0 || peer->rank >= peer->world || peer->world > 32)
+      return fail(CC1D_ERR_INVALID_ARGUMENT, "cc1d_bwd_peer_reduce: rank %d / world %d invalid (world <= 32)",
+                  peer->rank, peer->world);
+    if (p->dim > 0 && (!peer->exchange || !peer->flags || !peer->epochs))
+      return fail(CC1D_ERR_INVALID_ARGUMENT, "cc1d_bwd_peer_reduce: exchange, flags and epochs are required");
+  }
   if (p->dim == 0) return ok();
+  if ((rc = bind_device(p->dwdb_acc, "cc1d_bwd")) != CC1D_OK) return rc;
   Plan plan;
   std::memset(&plan, 0, sizeof(plan));
   cudaError_t e = cudaSuccess;
@@ -235,10 +293,30 @@ int cc1d_bwd(const cc1d_bwd_params* p, void* stream) {
   FinalizeArgs f{static_cast<const float*>(p->workspace), plan.n_partials, p->dim, p->dwdb_acc,
                  p->dweight_out, p->dweight_dim_stride, p->dweight_width_stride,
                  p->dbias_out, p->dbias_stride, p->bias != nullptr ? 1 : 0};
-  e = launch_finalize(p->dtype, p->width, f, s);
-  if (e != cudaSuccess) return cuda_fail(e, "cc1d_bwd finalize launch");
+  if (peer == nullptr) {
+    e = launch_finalize(p->dtype, p->width, f, s);
+    if (e != cudaSuccess) return cuda_fail(e, "cc1d_bwd finalize launch");
+  } else {
+    PeerFinalizeArgs pf{f, peer->rank, peer->world, peer->exchange, peer->flags, peer->epochs,
+                        peer_blocks(p->dim, p->width)};
+    e = launch_finalize_peer(p->dtype, p->width, pf, s);
+    if (e != cudaSuccess) return cuda_fail(e, "cc1d_bwd_peer_reduce finalize launch");
+  }
   return ok();
 }
+
+}  // namespace
+
+extern "C" {
+
+int cc1d_bwd(const cc1d_bwd_params* p, void* stream) { return bwd_impl(p, nullptr, stream); }
+
+int cc1d_bwd_peer_reduce(const cc1d_bwd_params* p, const cc1d_peer_reduce* peer, void* stream) {
+  if (peer == nullptr) return fail(CC1D_ERR_INVALID_ARGUMENT, "cc1d_bwd_peer_reduce: peer is NULL");
+  return bwd_impl(p, peer, stream);
+}
+
+int64_t cc1d_peer_blocks(int64_t dim, int32_t width) { return dim <= 0 ? 0 : peer_blocks(dim, width); }
 
 int cc1d_update(const cc1d_update_params* p, void* stream) {
   if (p == nullptr) return fail(CC1D_ERR_INVALID_ARGUMENT, "cc1d_update: params is NULL");
@@ -257,6 +335,8 @@ int cc1d_update(const cc1d_update_params* p, void* stream) {
   if (p->conv_state_indices == nullptr && p->state_rows < p->batch)
     return fail(CC1D_ERR_INVALID_ARGUMENT, "cc1d_update: conv_state has %lld rows for batch %lld",
                 (long long)p->state_rows, (long long)p->batch);
+  int rc = bind_device(p->out, "cc1d_update");
+  if (rc != CC1D_OK) return rc;
   UpdateArgs a{p->x, p->x_batch_stride, p->x_dim_stride, p->x_seq_stride,
                p->weight, p->weight_dim_stride, p->weight_width_stride,
                p->bias, p->bias_stride,
@@ -278,6 +358,8 @@ int cc1d_varlen_states(const cc1d_varlen_states_params* p, void* stream) {
   if (p->batch * p->dim * p->state_len == 0) return ok();
   if (!p->cu_seqlens || !p->states || (!p->x && p->total_tokens > 0))
     return fail(CC1D_ERR_INVALID_ARGUMENT, "cc1d_varlen_states: x, cu_seqlens and states are required");
+  int rc = bind_device(p->states, "cc1d_varlen_states");
+  if (rc != CC1D_OK) return rc;
   VarlenArgs a{p->x, p->x_token_stride, p->x_dim_stride, p->cu_seqlens,
                p->states, p->states_batch_stride, p->states_dim_stride, p->states_seq_stride,
                p->batch, p->dim, p->state_len, p->total_tokens};
@@ -289,6 +371,8 @@ int cc1d_varlen_states(const cc1d_varlen_states_params* p, void* stream) {
 int cc1d_device_status(unsigned* wait_timeouts) {
   if (wait_timeouts == nullptr) return fail(CC1D_ERR_INVALID_ARGUMENT, "cc1d_device_status: NULL output");
   cudaError_t e = read_wait_timeouts(wait_timeouts);
+  if (e != cudaSuccess) return cuda_fail(e, "cc1d_device_status");
+  e = read_peer_timeouts(wait_timeouts);
   if (e != cudaSuccess) return cuda_fail(e, "cc1d_device_status");
   return ok();
 }

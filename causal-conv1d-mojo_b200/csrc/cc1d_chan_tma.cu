@@ -539,9 +539,14 @@ bool make_map(CUtensorMap* m, const void* base, i64 D, i64 L, i64 B, i64 s_l, i6
   cuuint64_t strides[2] = {(cuuint64_t)(s_l * esz), (cuuint64_t)(s_b * esz)};
   cuuint32_t box[3] = {(cuuint32_t)kGroup, (cuuint32_t)rows, 1};
   cuuint32_t estr[3] = {1, 1, 1};
-  return enc(m, tma_dtype<T>(), 3, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-             CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+  const CUresult r = enc(m, tma_dtype<T>(), 3, const_cast<void*>(base), dims, strides, box, estr,
+                         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    set_error_detail("cuTensorMapEncodeTiled returned %d (dims %llu,%llu,%llu strides %llu,%llu)", (int)r,
+                     (unsigned long long)dims[0], (unsigned long long)dims[1], (unsigned long long)dims[2],
+                     (unsigned long long)strides[0], (unsigned long long)strides[1]);
+  return r == CUDA_SUCCESS;
 }
 
 bool aligned_to(const void* p, int bytes) { return (reinterpret_cast<uintptr_t>(p) % (uintptr_t)bytes) == 0; }
@@ -564,11 +569,17 @@ bool shape_ok(i64 B, i64 D, i64 L) {
 int esize(int dtype) { return dtype == 2 ? 4 : 2; }
 
 template <typename K>
-cudaError_t prepare(K kernel, size_t smem, std::atomic<int>& attr_done, std::atomic<int>& occ, int* nb) {
-  if (!attr_done.load(std::memory_order_acquire)) {
-    cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+cudaError_t prepare(K kernel, size_t smem, std::atomic<uint64_t>& attr_done, std::atomic<int>& occ, int* nb) {
+  // The shared-memory limit is a per-device (per-context) attribute: one
+  // bit per device that has it set.
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  const uint64_t bit = dev >= 0 && dev < 64 ? (1ull << dev) : 0ull;
+  if (bit == 0 || !(attr_done.load(std::memory_order_acquire) & bit)) {
+    e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
-    attr_done.store(1, std::memory_order_release);
+    attr_done.fetch_or(bit, std::memory_order_acq_rel);
   }
   return blocks_per_sm(kernel, kThreadsTma, smem, occ, nb);
 }
@@ -592,7 +603,8 @@ void split_rows(const DeviceInfo& dev, int nb, i64 D, i64 R, int tile_rows, Plan
 template <typename T, int W, bool SEQ, bool SILU>
 cudaError_t fwd_instance(FwdTmaParams* prm, const Plan* plan, cudaStream_t stream, int* nb_out) {
   constexpr size_t smem = (size_t)kFwdStages * fwd_rows<T>() * kGroup * sizeof(T) + 2 * kFwdStages * sizeof(uint64_t);
-  static std::atomic<int> attr{0}, occ{0};
+  static std::atomic<uint64_t> attr{0};
+  static std::atomic<int> occ{0};
   int nb = 1;
   cudaError_t e = prepare(fwd_chan_tma_kernel<T, W, SEQ, SILU>, smem, attr, occ, &nb);
   if (e != cudaSuccess) return e;
@@ -605,7 +617,8 @@ cudaError_t fwd_instance(FwdTmaParams* prm, const Plan* plan, cudaStream_t strea
 template <typename T, int W, bool SEQ, bool SILU>
 cudaError_t bwd_instance(BwdTmaParams* prm, const Plan* plan, cudaStream_t stream, int* nb_out) {
   constexpr size_t smem = (size_t)kBwdStages * 2 * bwd_rows<T>() * kGroup * sizeof(T) + 2 * kBwdStages * sizeof(uint64_t);
-  static std::atomic<int> attr{0}, occ{0};
+  static std::atomic<uint64_t> attr{0};
+  static std::atomic<int> occ{0};
   int nb = 1;
   cudaError_t e = prepare(bwd_chan_tma_kernel<T, W, SEQ, SILU>, smem, attr, occ, &nb);
   if (e != cudaSuccess) return e;

@@ -72,6 +72,16 @@ struct FinalizeArgs {
   int has_bias;
 };
 
+// Cross-GPU reduction of the dweight/dbias partials (cc1d_peer.cu).
+struct PeerFinalizeArgs {
+  FinalizeArgs f;
+  int rank, world;
+  float* const* bufs;      // device array [world] of exchange buffers (2 * D*(W+1) floats each)
+  uint32_t* const* flags;  // device array [world] of flag arrays (world * nblocks each)
+  uint32_t* epochs;        // this rank's per-block call counters (nblocks)
+  i64 nblocks;
+};
+
 struct UpdateArgs {
   const void* x; i64 xs_b, xs_c, xs_l;
   const void* w; i64 ws_c, ws_k;
@@ -131,10 +141,17 @@ cudaError_t plan_bwd_seq_tma(int dtype, int width, const BwdArgs& a, Plan* plan)
 cudaError_t launch_bwd_seq_tma(int dtype, int width, const BwdArgs& a, const Plan& plan, cudaStream_t stream);
 cudaError_t read_seq_wait_timeouts(unsigned* count);
 
+i64 peer_blocks(i64 dim, int width);
+cudaError_t launch_finalize_peer(int dtype, int width, const PeerFinalizeArgs& p, cudaStream_t stream);
+cudaError_t read_peer_timeouts(unsigned* count);
+
 // Records a message for cc1d_last_error() and returns `code` (for entry
 // points defined outside cc1d_abi.cu).
 int report_error(int code, const char* fmt, ...);
 int report_cuda_error(cudaError_t e, const char* what);
+// Extra text for the next CUDA error message of this thread (e.g. why a
+// tensor map could not be encoded).
+void set_error_detail(const char* fmt, ...);
 
 // Reads and clears the device-side count of bounded waits that gave up.
 cudaError_t read_wait_timeouts(unsigned* count);

@@ -495,9 +495,14 @@ bool make_seq_map(CUtensorMap* m, const void* base, i64 L, i64 D, i64 B, i64 s_c
   cuuint64_t strides[2] = {(cuuint64_t)(s_c * esz), (cuuint64_t)(s_b * esz)};
   cuuint32_t box[3] = {(cuuint32_t)kTL, (cuuint32_t)kRows, 1};
   cuuint32_t estr[3] = {1, 1, 1};
-  return enc(m, tma_dtype<T>(), 3, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-             CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+  const CUresult r = enc(m, tma_dtype<T>(), 3, const_cast<void*>(base), dims, strides, box, estr,
+                         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    set_error_detail("cuTensorMapEncodeTiled returned %d (dims %llu,%llu,%llu strides %llu,%llu)", (int)r,
+                     (unsigned long long)dims[0], (unsigned long long)dims[1], (unsigned long long)dims[2],
+                     (unsigned long long)strides[0], (unsigned long long)strides[1]);
+  return r == CUDA_SUCCESS;
 }
 
 bool aligned_to(const void* p, int bytes) { return (reinterpret_cast<uintptr_t>(p) % (uintptr_t)bytes) == 0; }
@@ -515,11 +520,17 @@ bool seq_shape_ok(i64 B, i64 D, i64 L) {
 int esize(int dtype) { return dtype == 2 ? 4 : 2; }
 
 template <typename K>
-cudaError_t prepare(K kernel, size_t smem, std::atomic<int>& attr_done, std::atomic<int>& occ, int* nb) {
-  if (!attr_done.load(std::memory_order_acquire)) {
-    cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+cudaError_t prepare(K kernel, size_t smem, std::atomic<uint64_t>& attr_done, std::atomic<int>& occ, int* nb) {
+  // The shared-memory limit is a per-device (per-context) attribute: one
+  // bit per device that has it set.
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  const uint64_t bit = dev >= 0 && dev < 64 ? (1ull << dev) : 0ull;
+  if (bit == 0 || !(attr_done.load(std::memory_order_acquire) & bit)) {
+    e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
-    attr_done.store(1, std::memory_order_release);
+    attr_done.fetch_or(bit, std::memory_order_acq_rel);
   }
   return blocks_per_sm(kernel, kThreadsSeq, smem, occ, nb);
 }
@@ -549,7 +560,8 @@ void seq_schedule(const DeviceInfo& dev, int nb, i64 B, i64 D, i64 L, Plan* plan
 template <typename T, int W, bool SILU>
 cudaError_t seq_fwd_instance(SeqFwdParams* prm, const Plan* plan, cudaStream_t stream, int* nb_out) {
   constexpr size_t smem = (size_t)seq_fwd_stages<T>() * seq_tile_bytes<T>() + 2 * seq_fwd_stages<T>() * sizeof(uint64_t);
-  static std::atomic<int> attr{0}, occ{0};
+  static std::atomic<uint64_t> attr{0};
+  static std::atomic<int> occ{0};
   int nb = 1;
   cudaError_t e = prepare(fwd_seq_tma_kernel<T, W, SILU>, smem, attr, occ, &nb);
   if (e != cudaSuccess) return e;
@@ -563,7 +575,8 @@ template <typename T, int W, bool SILU>
 cudaError_t seq_bwd_instance(SeqBwdParams* prm, const Plan* plan, cudaStream_t stream, int* nb_out) {
   constexpr size_t smem =
       (size_t)seq_bwd_stages<T>() * 2 * seq_tile_bytes<T>() + 2 * seq_bwd_stages<T>() * sizeof(uint64_t);
-  static std::atomic<int> attr{0}, occ{0};
+  static std::atomic<uint64_t> attr{0};
+  static std::atomic<int> occ{0};
   int nb = 1;
   cudaError_t e = prepare(bwd_seq_tma_kernel<T, W, SILU>, smem, attr, occ, &nb);
   if (e != cudaSuccess) return e;

@@ -92,6 +92,7 @@ STRUCTS = {
     "cc1d_bwd_params": _lib.BwdParams,
     "cc1d_update_params": _lib.UpdateParams,
     "cc1d_varlen_states_params": _lib.VarlenParams,
+    "cc1d_peer_reduce": _lib.PeerReduceParams,
 }
 
 

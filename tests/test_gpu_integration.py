@@ -133,3 +133,52 @@ def test_pipeline_waits_never_time_out():
         out, fs = causal_conv1d_fn(x, w, initial_states=init, return_final_states=True, activation="silu")
         torch.autograd.backward([out, fs], [torch.randn_like(out), torch.randn_like(fs)])
     assert _lib.device_wait_timeouts() == 0
+
+
+@pytest.mark.parametrize("layout", ["chanlast", "contig"])
+def test_calls_from_a_fresh_host_thread(layout):
+    """A host thread that no framework ever bound to a device (as an autograd
+    worker thread of device 0 can be): the first call there goes straight to
+    a TMA kernel whose launch setup is already cached, so the library itself
+    must bind the device's context before encoding tensor maps.  Results
+    equal the main thread's bitwise."""
+    import threading
+
+    from causal_conv1d_b200 import _ops
+
+    B, D, L, W = 2, 512, 256, 4
+    g = torch.Generator(device="cpu").manual_seed(3)
+
+    def mk(*s):
+        return torch.randn(*s, generator=g).to(torch.bfloat16).to(DEV)
+
+    if layout == "chanlast":
+        x, dout = mk(B, L, D).transpose(1, 2), mk(B, L, D).transpose(1, 2)
+    else:
+        x, dout = mk(B, D, L), mk(B, D, L)
+    w, b = mk(D, W), mk(D)
+
+    def run():
+        out = torch.empty_like(x)
+        dx = torch.empty_like(x)
+        dwdb = torch.empty(D * (W + 1), dtype=torch.float32, device=DEV)
+        _ops.fwd(x, w, b, None, None, out, True, None)
+        _ops.bwd(x, w, b, dout, None, None, None, dx, dwdb, None, None, None, True)
+        torch.cuda.synchronize()
+        return out, dx, dwdb
+
+    main = run()  # warms every launch cache on this thread
+    got, errors = [], []
+
+    def worker():
+        try:
+            got.append(run())
+        except Exception as e:  # reported below
+            errors.append(e)
+
+    t = threading.Thread(target=worker)
+    t.start()
+    t.join()
+    assert not errors, errors
+    for a, c in zip(main, got[0]):
+        assert torch.equal(a, c)

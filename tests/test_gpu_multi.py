@@ -1,0 +1,231 @@
+"""Batch-sharded backward on several GPUs, one process per GPU over NCCL:
+the dweight/dbias reduction fused with the cross-GPU sum over NVLink peer
+memory (cc1d_bwd_peer_reduce through parallel.PeerReducer).
+
+Checked on every rank, for every call of a sequence (so both halves of the
+double-buffered exchange and stale-data hazards are exercised), eagerly and
+replayed from a CUDA graph:
+
+* fp32 [dweight | dbias] is bitwise equal to the rank-order sum of the
+  per-rank cc1d_bwd results (gathered with NCCL),
+* the parameter-dtype dweight / dbias are that sum rounded once,
+* dx / dinitial_states equal the single-GPU kernel's bitwise,
+* the autograd path (causal_conv1d_fn_batch_sharded with a reducer) matches
+  the unsharded causal_conv1d_fn within the dtype tolerance,
+* no bounded wait gave up.
+
+Needs two or more GPUs (one rank per GPU; two ranks on one GPU are refused
+by PeerReducer); skipped otherwise."""
+
+from __future__ import annotations
+
+import datetime
+import os
+import socket
+import sys
+import traceback
+from pathlib import Path
+
+import pytest
+import torch
+
+REPO = Path(__file__).resolve().parent.parent
+
+pytestmark = pytest.mark.gpu
+
+WORLD = min(torch.cuda.device_count(), 4) if torch.cuda.is_available() else 0
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    return port
+
+
+def _case_inputs(dtype, B, D, L, W, seed, has_bias, chanlast):
+    g = torch.Generator("cpu").manual_seed(seed)
+
+    def lay(t):
+        return t.transpose(1, 2).contiguous().transpose(1, 2) if chanlast else t.contiguous()
+
+    x = lay(torch.randn(B, D, L, generator=g).to(dtype))
+    w = (torch.rand(D, W, generator=g) - 0.5).to(dtype)
+    b = (torch.rand(D, generator=g) - 0.5).to(dtype) if has_bias else None
+    init = torch.randn(B, D, W - 1, generator=g).to(dtype)
+    douts = [lay(torch.randn(B, D, L, generator=g).to(dtype)) for _ in range(4)]
+    return x, w, b, init, douts
+
+
+CASES = [
+    # dtype, rows per rank, D, L, W, bias, channel-last
+    (torch.bfloat16, 2, 512, 256, 4, True, True),
+    (torch.float32, 1, 200, 77, 3, False, False),
+    (torch.float16, 3, 96, 128, 2, True, True),
+]
+
+
+def _run_case(case, rank, world, dev):
+    import torch.distributed as dist
+
+    from causal_conv1d_b200 import _lib, _ops, causal_conv1d_fn
+    from causal_conv1d_b200.parallel import PeerReducer, causal_conv1d_fn_batch_sharded, shard_range
+
+    dtype, per, D, L, W, has_bias, chanlast = case
+    B = per * world
+    x, w, b, init, douts = _case_inputs(dtype, B, D, L, W, 17 + D, has_bias, chanlast)
+    b0, b1 = shard_range(B, rank, world)
+    to = dict(device=dev)
+    xs, ws = x[b0:b1].to(**to), w.to(**to)
+    bs = b.to(**to) if b is not None else None
+    inits = init[b0:b1].to(**to)
+    douts_s = [d[b0:b1].to(**to) for d in douts]
+
+    def local(dout):
+        dx = torch.empty_like(xs)
+        dwdb = torch.empty(D * (W + 1), dtype=torch.float32, **to)
+        dinit = torch.empty_like(inits)
+        _ops.bwd(xs, ws, bs, dout, None, inits, None, dx, dwdb, dinit, None, None, True)
+        parts = [torch.empty_like(dwdb) for _ in range(world)]
+        dist.all_gather(parts, dwdb)
+        total = torch.zeros_like(dwdb)
+        for p in parts:
+            total = total + p
+        return dx, dinit, total
+
+    reducer = PeerReducer(D, W, dev)
+    try:
+        dx = torch.empty_like(xs)
+        dwdb = torch.empty(D * (W + 1), dtype=torch.float32, **to)
+        dinit = torch.empty_like(inits)
+        dw = torch.empty(D, W, dtype=dtype, **to)
+        db = torch.empty(D, dtype=dtype, **to) if has_bias else None
+        static_dout = torch.empty_like(douts_s[0])
+
+        def peer():
+            _ops.bwd_peer(xs, ws, bs, static_dout, inits, None, dx, dwdb, dinit, dw, db, True, *reducer.args())
+
+        def check(i, how):
+            ref_dx, ref_dinit, total = local(douts_s[i])
+            tag = f"{how} call {i} rank {rank}"
+            assert torch.equal(dwdb, total), tag
+            assert torch.equal(dw, total[: D * W].view(D, W).to(dtype)), tag
+            if has_bias:
+                assert torch.equal(db, total[D * W:].to(dtype)), tag
+            else:
+                assert torch.count_nonzero(dwdb[D * W:]) == 0, tag
+            assert torch.equal(dx, ref_dx), tag
+            assert torch.equal(dinit, ref_dinit), tag
+
+        # Eager: four calls in a row with different gradients.
+        for i in range(4):
+            static_dout.copy_(douts_s[i])
+            peer()
+            check(i, "eager")
+        # Replayed from a CUDA graph: the call counters advance on the device.
+        torch.cuda.synchronize(dev)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            peer()
+        for i in (1, 3, 0, 2, 2):
+            static_dout.copy_(douts_s[i])
+            g.replay()
+            check(i, "graph")
+        del g
+
+        # Autograd through the public batch-sharded function vs unsharded.
+        xa = xs.clone().requires_grad_()
+        wa = ws.clone().requires_grad_()
+        ba = bs.clone().requires_grad_() if bs is not None else None
+        out = causal_conv1d_fn_batch_sharded(xa, wa, ba, activation="silu", reducer=reducer)
+        out.backward(douts_s[0])
+        xf = x.to(**to).requires_grad_()
+        wf = w.to(**to).requires_grad_()
+        bf = b.to(**to).requires_grad_() if b is not None else None
+        outf = causal_conv1d_fn(xf, wf, bf, activation="silu")
+        outf.backward(douts[0].to(**to))
+        tol = dict(rtol=1e-5, atol=1e-5) if dtype == torch.float32 else dict(rtol=1e-2, atol=1e-2)
+        torch.testing.assert_close(out, outf[b0:b1].detach(), **tol)
+        torch.testing.assert_close(xa.grad, xf.grad[b0:b1], **tol)
+        # dweight sums B*L products: compare against the fp32 reduction.
+        torch.testing.assert_close(wa.grad.float(), wf.grad.float(), rtol=tol["rtol"], atol=tol["atol"] * 10)
+        if ba is not None:
+            torch.testing.assert_close(ba.grad.float(), bf.grad.float(), rtol=tol["rtol"], atol=tol["atol"] * 10)
+        torch.cuda.synchronize(dev)
+        assert _lib.device_wait_timeouts() == 0
+    finally:
+        reducer.close()
+
+
+def _worker(rank, world, port, q):
+    sys.path[:0] = [str(REPO), str(REPO / "causal-conv1d-mojo_b200")]
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    import torch.distributed as dist
+
+    dev = torch.device("cuda", rank)
+    torch.cuda.set_device(dev)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
+                            device_id=dev)
+    case = None
+    try:
+        for case in CASES:
+            _run_case(case, rank, world, dev)
+        q.put((rank, "ok", ""))
+    except Exception:  # reported to the parent
+        q.put((rank, "fail", f"case {case}\n" + traceback.format_exc()))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(WORLD < 2, reason="needs two or more GPUs")
+def test_peer_reduce_matches_rank_order_sum():
+    import torch.multiprocessing as mp
+
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, WORLD, port, q)) for r in range(WORLD)]
+    for p in procs:
+        p.start()
+    results = {}
+    try:
+        for _ in range(WORLD):
+            rank, status, msg = q.get(timeout=600)
+            results[rank] = (status, msg)
+    finally:
+        for p in procs:
+            p.join(timeout=120)
+            if p.is_alive():
+                p.kill()
+    bad = [f"rank {r}:\n{m}" for r, (s, m) in sorted(results.items()) if s != "ok"]
+    if bad:
+        pytest.fail("\n".join(bad), pytrace=False)
+    assert len(results) == WORLD
+
+
+@pytest.mark.skipif(WORLD < 2, reason="needs two or more GPUs")
+def test_one_process_several_devices():
+    """One process driving every GPU in turn (highest index first), forward
+    and autograd backward: per-device kernel attributes and the device the
+    library launches on follow the data, whichever device the calling thread
+    was bound to.  All devices give bitwise identical results."""
+    from causal_conv1d_b200 import causal_conv1d_fn
+
+    B, D, L, W = 2, 512, 256, 4
+    x, w, b, init, douts = _case_inputs(torch.bfloat16, B, D, L, W, 5, True, True)
+    results = []
+    torch.cuda.set_device(0)
+    for d in reversed(range(WORLD)):
+        dev = torch.device("cuda", d)
+        xd = x.to(dev).requires_grad_()
+        wd = w.to(dev).requires_grad_()
+        bd = b.to(dev).requires_grad_()
+        out = causal_conv1d_fn(xd, wd, bd, activation="silu")
+        out.backward(douts[0].to(dev))
+        torch.cuda.synchronize(dev)
+        results.append([t.cpu() for t in (out, xd.grad, wd.grad, bd.grad)])
+    for other in results[1:]:
+        for a, c in zip(results[0], other):
+            assert torch.equal(a, c)
