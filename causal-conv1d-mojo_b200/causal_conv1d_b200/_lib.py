@@ -97,7 +97,7 @@ class VarlenParams(ctypes.Structure):
 
 
 class PeerReduceParams(ctypes.Structure):
-    _fields_ = [("rank", c_i32), ("world", c_i32), ("exchange", c_ptr), ("flags", c_ptr), ("epochs", c_ptr)]
+    _fields_ = [("rank", c_i32), ("world", c_i32), ("exchange", c_ptr), ("epochs", c_ptr)]
 
 
 # Every symbol include/cc1d.h declares, with its ctypes signature.
@@ -108,6 +108,7 @@ SIGNATURES = {
     "cc1d_bwd_noalloc": (c_i32, [ctypes.POINTER(BwdParams), c_ptr]),
     "cc1d_bwd_peer_reduce": (c_i32, [ctypes.POINTER(BwdParams), ctypes.POINTER(PeerReduceParams), c_ptr]),
     "cc1d_peer_blocks": (c_i64, [c_i64, c_i32]),
+    "cc1d_peer_exchange_bytes": (c_i64, [c_i64, c_i32, c_i32]),
     "cc1d_update": (c_i32, [ctypes.POINTER(UpdateParams), c_ptr]),
     "cc1d_varlen_states": (c_i32, [ctypes.POINTER(VarlenParams), c_ptr]),
     "cc1d_device_status": (c_i32, [ctypes.POINTER(ctypes.c_uint)]),

@@ -219,21 +219,20 @@ def _bwd_peer_impl(
     dbias_out: torch.Tensor | None,
     apply_silu: bool,
     exchange_ptrs: torch.Tensor,
-    flag_ptrs: torch.Tensor,
     epochs: torch.Tensor,
     rank: int,
     world: int,
 ) -> None:
     """Backward of a batch shard with dweight/dbias summed over `world` ranks
-    in the same kernel (cc1d_bwd_peer_reduce).  exchange_ptrs / flag_ptrs:
-    int64 device tensors of the ranks' peer-mapped buffer addresses."""
+    in the same kernel (cc1d_bwd_peer_reduce).  exchange_ptrs: int64 device
+    tensor of the ranks' peer-mapped exchange buffer addresses."""
     _require_cuda(x, "causal_conv1d_fn backward (peer reduce)")
     lib = _lib.load()
     p = _bwd_params(x, weight, bias, dout, None, initial_states, dfinal_states, dx, dwdb_acc, dinitial_states,
                     dweight_out, dbias_out, apply_silu)
     q = _lib.PeerReduceParams()
     q.rank, q.world = rank, world
-    q.exchange, q.flags, q.epochs = exchange_ptrs.data_ptr(), flag_ptrs.data_ptr(), epochs.data_ptr()
+    q.exchange, q.epochs = exchange_ptrs.data_ptr(), epochs.data_ptr()
     with _on_device(x.device):
         nbytes = bwd_workspace_bytes(p)
         ws = None
@@ -247,7 +246,7 @@ def _bwd_peer_impl(
 
 
 def _bwd_peer_fake(x, weight, bias, dout, initial_states, dfinal_states, dx, dwdb_acc, dinitial_states,
-                   dweight_out, dbias_out, apply_silu, exchange_ptrs, flag_ptrs, epochs, rank, world) -> None:
+                   dweight_out, dbias_out, apply_silu, exchange_ptrs, epochs, rank, world) -> None:
     return None
 
 

@@ -75,17 +75,19 @@ def _rt_check(res, what: str):
 
 
 class PeerReducer:
-    """Peer-mapped buffers for the fused backward reduction over `group`
-    (one process per GPU, all GPUs of one node).
+    """Peer-mapped exchange buffers for the fused backward reduction over
+    `group` (one process per GPU, all GPUs of one node).
 
-    Each rank cudaMallocs an exchange buffer (2*dim*(width+1) fp32: one half
-    per call parity) and a flag array (world * cc1d_peer_blocks(dim, width)
-    uint32), exports them as CUDA IPC handles, gathers the peers' handles
-    over `group` and maps them.  Plain peer memory -- no multicast object.
-    Construction and ``close()`` are collective over `group`; every rank must
-    then issue the same sequence of backward calls with the same dim/width.
-    The per-block call counters live on the device, so those calls may be
-    captured in a CUDA graph and replayed.
+    Each rank cudaMallocs one exchange buffer of
+    cc1d_peer_exchange_bytes(dim, width, world) bytes (8-byte {call tag,
+    value} words, two halves alternating by call parity), exports it as a
+    CUDA IPC handle, gathers the peers' handles over `group` and maps them;
+    the kernel stores every rank's partial sums straight into every peer's
+    buffer.  Plain peer memory -- no multicast object.  Construction and
+    ``close()`` are collective over `group`; every rank must then issue the
+    same sequence of backward calls with the same dim/width.  The per-block
+    call counters live on the device, so those calls may be captured in a
+    CUDA graph and replayed.
     """
 
     def __init__(self, dim: int, width: int, device: torch.device | str | int | None = None, group=None):
@@ -105,49 +107,44 @@ class PeerReducer:
         if dev.index is None:
             dev = torch.device("cuda", torch.cuda.current_device())
         self.device, self.dim, self.width = dev, dim, width
-        self.nblocks = int(_lib.load().cc1d_peer_blocks(dim, width))
-        ex_bytes = max(2 * dim * (width + 1) * 4, 16)
-        fl_bytes = max(self.world * self.nblocks * 4, 16)
+        lib = _lib.load()
+        self.nblocks = int(lib.cc1d_peer_blocks(dim, width))
+        nbytes = max(int(lib.cc1d_peer_exchange_bytes(dim, width, self.world)), 16)
         _rt_check(rt.cudaSetDevice(dev.index), "cudaSetDevice")
-        self._own = [_rt_check(rt.cudaMalloc(ex_bytes), "cudaMalloc"), _rt_check(rt.cudaMalloc(fl_bytes), "cudaMalloc")]
-        _rt_check(rt.cudaMemset(self._own[0], 0, ex_bytes), "cudaMemset")
-        _rt_check(rt.cudaMemset(self._own[1], 0, fl_bytes), "cudaMemset")
+        self._own = _rt_check(rt.cudaMalloc(nbytes), "cudaMalloc")
+        _rt_check(rt.cudaMemset(self._own, 0, nbytes), "cudaMemset")
         _rt_check(rt.cudaDeviceSynchronize(), "cudaDeviceSynchronize")
-        handles = [bytes(_rt_check(rt.cudaIpcGetMemHandle(p), "cudaIpcGetMemHandle").reserved) for p in self._own]
+        handle = bytes(_rt_check(rt.cudaIpcGetMemHandle(self._own), "cudaIpcGetMemHandle").reserved)
         uuid = str(torch.cuda.get_device_properties(dev).uuid)
         gathered: list = [None] * self.world
-        dist.all_gather_object(gathered, (uuid, handles), group=group)
+        dist.all_gather_object(gathered, (uuid, handle), group=group)
         if len({g[0] for g in gathered}) != self.world:
             # The reduction kernels of different ranks wait for one another;
             # two of them queued on one GPU are not guaranteed to run together.
-            for p in self._own:
-                rt.cudaFree(p)
+            rt.cudaFree(self._own)
             self._own = None
             raise ValueError("PeerReducer needs one GPU per rank (two ranks share a device)")
-        gathered = [g[1] for g in gathered]
         self._mapped = []
-        ptrs = [[0] * self.world, [0] * self.world]
-        for r in range(self.world):
-            for j in range(2):
-                if r == self.rank:
-                    ptrs[j][r] = int(self._own[j])
-                    continue
-                h = rt.cudaIpcMemHandle_t()
-                h.reserved = gathered[r][j]
-                mp = _rt_check(rt.cudaIpcOpenMemHandle(h, rt.cudaIpcMemLazyEnablePeerAccess), "cudaIpcOpenMemHandle")
-                self._mapped.append(mp)
-                ptrs[j][r] = int(mp)
-        self.exchange_ptrs = torch.tensor(ptrs[0], dtype=torch.int64, device=dev)
-        self.flag_ptrs = torch.tensor(ptrs[1], dtype=torch.int64, device=dev)
+        ptrs = [0] * self.world
+        for r, (_, h_bytes) in enumerate(gathered):
+            if r == self.rank:
+                ptrs[r] = int(self._own)
+                continue
+            h = rt.cudaIpcMemHandle_t()
+            h.reserved = h_bytes
+            mp = _rt_check(rt.cudaIpcOpenMemHandle(h, rt.cudaIpcMemLazyEnablePeerAccess), "cudaIpcOpenMemHandle")
+            self._mapped.append(mp)
+            ptrs[r] = int(mp)
+        self.exchange_ptrs = torch.tensor(ptrs, dtype=torch.int64, device=dev)
         self.epochs = torch.zeros(max(self.nblocks, 1), dtype=torch.int32, device=dev)
         torch.cuda.synchronize(dev)
         dist.barrier(group=group)
 
-    def args(self) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor, int, int]:
-        """(exchange_ptrs, flag_ptrs, epochs, rank, world) for ``_ops.bwd_peer``."""
+    def args(self) -> tuple[torch.Tensor, torch.Tensor, int, int]:
+        """(exchange_ptrs, epochs, rank, world) for ``_ops.bwd_peer``."""
         if self._own is None:
             raise RuntimeError("PeerReducer is closed")
-        return self.exchange_ptrs, self.flag_ptrs, self.epochs, self.rank, self.world
+        return self.exchange_ptrs, self.epochs, self.rank, self.world
 
     def close(self) -> None:
         """Collective: unmap the peers' buffers, then free this rank's."""
@@ -160,9 +157,8 @@ class PeerReducer:
         for mp in self._mapped:
             _rt_check(rt.cudaIpcCloseMemHandle(mp), "cudaIpcCloseMemHandle")
         self._mapped = []
-        dist.barrier(group=self.group)  # every peer has unmapped this rank's buffers
-        for p in self._own:
-            _rt_check(rt.cudaFree(p), "cudaFree")
+        dist.barrier(group=self.group)  # every peer has unmapped this rank's buffer
+        _rt_check(rt.cudaFree(self._own), "cudaFree")
         self._own = None
 
     def __enter__(self):

@@ -266,8 +266,8 @@ int bwd_impl(const cc1d_bwd_params* p, const cc1d_peer_reduce* peer, void* strea
     if (peer->world < 1 || peer->rank < 0 || peer->rank >= peer->world || peer->world > 32)
       return fail(CC1D_ERR_INVALID_ARGUMENT, "cc1d_bwd_peer_reduce: rank %d / world %d invalid (world <= 32)",
                   peer->rank, peer->world);
-    if (p->dim > 0 && (!peer->exchange || !peer->flags || !peer->epochs))
-      return fail(CC1D_ERR_INVALID_ARGUMENT, "cc1d_bwd_peer_reduce: exchange, flags and epochs are required");
+    if (p->dim > 0 && (!peer->exchange || !peer->epochs))
+      return fail(CC1D_ERR_INVALID_ARGUMENT, "cc1d_bwd_peer_reduce: exchange and epochs are required");
   }
   if (p->dim == 0) return ok();
   if ((rc = bind_device(p->dwdb_acc, "cc1d_bwd")) != CC1D_OK) return rc;
@@ -297,8 +297,7 @@ int bwd_impl(const cc1d_bwd_params* p, const cc1d_peer_reduce* peer, void* strea
     e = launch_finalize(p->dtype, p->width, f, s);
     if (e != cudaSuccess) return cuda_fail(e, "cc1d_bwd finalize launch");
   } else {
-    PeerFinalizeArgs pf{f, peer->rank, peer->world, peer->exchange, peer->flags, peer->epochs,
-                        peer_blocks(p->dim, p->width)};
+    PeerFinalizeArgs pf{f, peer->rank, peer->world, peer->exchange, peer->epochs, peer_blocks(p->dim, p->width)};
     e = launch_finalize_peer(p->dtype, p->width, pf, s);
     if (e != cudaSuccess) return cuda_fail(e, "cc1d_bwd_peer_reduce finalize launch");
   }
@@ -317,6 +316,10 @@ int cc1d_bwd_peer_reduce(const cc1d_bwd_params* p, const cc1d_peer_reduce* peer,
 }
 
 int64_t cc1d_peer_blocks(int64_t dim, int32_t width) { return dim <= 0 ? 0 : peer_blocks(dim, width); }
+
+int64_t cc1d_peer_exchange_bytes(int64_t dim, int32_t width, int32_t world) {
+  return dim <= 0 || world <= 0 ? 0 : peer_exchange_bytes(dim, width, world);
+}
 
 int cc1d_update(const cc1d_update_params* p, void* stream) {
   if (p == nullptr) return fail(CC1D_ERR_INVALID_ARGUMENT, "cc1d_update: params is NULL");

@@ -76,9 +76,8 @@ struct FinalizeArgs {
 struct PeerFinalizeArgs {
   FinalizeArgs f;
   int rank, world;
-  float* const* bufs;      // device array [world] of exchange buffers (2 * D*(W+1) floats each)
-  uint32_t* const* flags;  // device array [world] of flag arrays (world * nblocks each)
-  uint32_t* epochs;        // this rank's per-block call counters (nblocks)
+  unsigned long long* const* bufs;  // device array [world] of exchange buffers
+  uint32_t* epochs;                 // this rank's per-block call counters (nblocks)
   i64 nblocks;
 };
 
@@ -142,6 +141,7 @@ cudaError_t launch_bwd_seq_tma(int dtype, int width, const BwdArgs& a, const Pla
 cudaError_t read_seq_wait_timeouts(unsigned* count);
 
 i64 peer_blocks(i64 dim, int width);
+i64 peer_exchange_bytes(i64 dim, int width, int world);
 cudaError_t launch_finalize_peer(int dtype, int width, const PeerFinalizeArgs& p, cudaStream_t stream);
 cudaError_t read_peer_timeouts(unsigned* count);
 

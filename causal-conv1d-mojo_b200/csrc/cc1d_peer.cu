@@ -5,23 +5,27 @@
 // of the fp32 [dweight | dbias] buffer -> casts.  The outputs are cut into
 // chunks of 32; block b owns chunks b, b + grid, b + 2*grid, ...:
 //   1. for each of its chunks it sums the local partial slots (as
-//      finalize_kernel: 8 warps, fixed order) and writes the 32 sums into
-//      this rank's exchange buffer (peer-visible, double-buffered by call
-//      parity),
-//   2. publishes its flag to every rank (st.release.sys into the peer's flag
-//      array) and waits until block b of every rank has published
-//      (ld.acquire.sys; bounded wait),
-//   3. adds the ranks' sums of its chunks in rank order (loads from peer
-//      memory) and writes fp32 dwdb plus the parameter-dtype copies.
-// Every rank adds the same values in the same order, so all ranks hold
-// bitwise identical gradients, reproducible run to run.  The grid is capped
-// (kPeerMaxBlocks) far below what the SMs hold at once, so every block of
-// every rank is resident and the cross-GPU waits cannot starve; blocks never
-// wait for other blocks of their own GPU.  Call numbers ("epochs") live in
-// device memory, one per block, so the kernel can be captured in a CUDA
-// graph and replayed; all ranks must make the same sequence of calls.  The
-// exchange buffers and flags are plain device memory shared through CUDA
-// IPC (no multicast objects, no TMA on peer memory).
+//      finalize_kernel: 8 warps, fixed order) and pushes every sum to every
+//      rank as one 8-byte word {call tag, fp32 bits}: a plain store into the
+//      receiving rank's exchange buffer (this rank's row of it, in the half
+//      selected by the call's parity),
+//   2. polls its own exchange buffer until the words of every rank carry
+//      this call's tag (bounded wait), then adds the ranks' values in rank
+//      order and writes fp32 dwdb plus the parameter-dtype copies.
+// An aligned 8-byte store is seen whole or not at all, so value and tag
+// travel together: no fences, no flags, no remote loads; the exchange costs
+// one NVLink store latency.  The halves alternate by call parity, and a rank
+// can only start call c+2 after every peer has pushed call c+1, i.e. after
+// every peer has read call c -- so a word is never overwritten before it is
+// read.  Every rank adds the same values in the same order, so all ranks
+// hold bitwise identical gradients, reproducible run to run.
+//
+// The grid is capped (kPeerMaxBlocks) near what the SMs hold at once; blocks
+// wait only for the blocks of the same index on other GPUs, never for blocks
+// of their own GPU.  Call numbers live in device memory, one per block, so
+// the kernel can be captured in a CUDA graph and replayed; all ranks must
+// make the same sequence of calls.  Exchange buffers are plain device memory
+// shared through CUDA IPC (no multicast objects, no TMA on peer memory).
 #include "cc1d_dispatch.cuh"
 
 namespace cc1d {
@@ -29,36 +33,36 @@ namespace cc1d {
 namespace {
 
 constexpr int kPeerWarps = 8;
-constexpr i64 kPeerMaxBlocks = 256;      // <= 2 blocks per SM of a B200
-constexpr unsigned kPeerSpin = 1u << 22;  // polls (with back-off) before giving up
+constexpr i64 kPeerMaxBlocks = 1024;      // B200: 148 SMs x 8 blocks of 256 threads resident
+constexpr unsigned kPeerSpin = 1u << 22;  // polls per lane (with back-off) before giving up
 
 static __device__ unsigned int g_peer_timeouts = 0;
 
-__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
-  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+__device__ __forceinline__ void st_relaxed_sys_u64(unsigned long long* p, unsigned long long v) {
+  asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
 }
 
-__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
-  uint32_t v;
-  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+__device__ __forceinline__ unsigned long long ld_relaxed_sys_u64(const unsigned long long* p) {
+  unsigned long long v;
+  asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
   return v;
 }
 
 template <typename T, int W>
 __global__ void __launch_bounds__(kPeerWarps * 32) finalize_peer_kernel(const PeerFinalizeArgs p) {
   __shared__ float part[kPeerWarps][32];
-  __shared__ int all_arrived;
   const FinalizeArgs& a = p.f;
   const i64 n = a.D * (W + 1);
   const i64 nchunks = ceil_div(n, (i64)32);
   const int lane = threadIdx.x & 31;
   const int warp = threadIdx.x >> 5;
   uint32_t* ep = p.epochs + blockIdx.x;
-  const uint32_t epoch = *ep + 1;  // this call's number for this block
-  const i64 parity_off = (i64)(epoch & 1u) * n;
-  float* mine = p.bufs[p.rank] + parity_off;
+  const uint32_t epoch = *ep + 1;  // this call's number (tag) for this block
+  const unsigned long long tag = (unsigned long long)epoch << 32;
+  // Word (parity, source rank, output) of a receiving rank's buffer.
+  const i64 half = (i64)(epoch & 1u) * p.world * n;
 
-  // 1. Local sums of this block's chunks into the exchange buffer.
+  // 1. Local sums of this block's chunks, pushed to every rank.
   for (i64 ch = blockIdx.x; ch < nchunks; ch += gridDim.x) {
     const i64 e = ch * 32 + lane;
     float s = 0.f;
@@ -70,49 +74,38 @@ __global__ void __launch_bounds__(kPeerWarps * 32) finalize_peer_kernel(const Pe
       s = part[0][lane];
 #pragma unroll
       for (int w2 = 1; w2 < kPeerWarps; ++w2) s += part[w2][lane];
-      mine[e] = s;
+      const unsigned long long word = tag | __float_as_uint(s);
+      const i64 off = half + (i64)p.rank * n + e;
+      for (int r = 0; r < p.world; ++r) st_relaxed_sys_u64(p.bufs[r] + off, word);
     }
     __syncthreads();
   }
 
-  // 2. Publish, then wait for block blockIdx.x of every rank.
-  if (warp == 0) {
-    __threadfence_system();
-    __syncwarp();
-    if (lane < p.world) st_release_sys(p.flags[lane] + (i64)p.rank * p.nblocks + blockIdx.x, epoch);
+  // 2. Rank-order sums of this block's chunks, one chunk per warp at a time.
+  const unsigned long long* mine = p.bufs[p.rank] + half;
+  for (i64 ch0 = blockIdx.x; ch0 < nchunks; ch0 += (i64)kPeerWarps * gridDim.x) {
+    const i64 ch = ch0 + (i64)warp * gridDim.x;
+    const i64 e = ch * 32 + lane;
+    const bool active = ch < nchunks && e < n;
     bool ok = true;
-    if (lane < p.world) {
-      const uint32_t* f = p.flags[p.rank] + (i64)lane * p.nblocks + blockIdx.x;
-      unsigned i = 0;
-      while (ld_acquire_sys(f) < epoch) {
-        if (++i > kPeerSpin) {
-          ok = false;
-          break;
+    float t = 0.f;
+    if (active) {
+      unsigned polls = 0;
+      for (int r = 0; r < p.world && ok; ++r) {
+        unsigned long long w = ld_relaxed_sys_u64(mine + (i64)r * n + e);
+        while ((w & 0xffffffff00000000ull) != tag) {
+          if (++polls > kPeerSpin) {
+            ok = false;
+            break;
+          }
+          if (polls > 64) __nanosleep(64);
+          w = ld_relaxed_sys_u64(mine + (i64)r * n + e);
         }
-        if (i > 32) __nanosleep(128);
+        t += __uint_as_float((unsigned)(w & 0xffffffffull));
       }
     }
-    ok = __all_sync(kFull, ok);
-    if (lane == 0) {
-      all_arrived = ok ? 1 : 0;
-      if (!ok) atomicAdd(&g_peer_timeouts, 1u);
-      // Counted even after a timeout, so this rank's call numbers keep
-      // matching its peers'.
-      *ep = epoch;
-    }
-  }
-  __syncthreads();
-  if (!all_arrived) return;  // outputs stay unwritten; the host reads the count
-  // Every thread acquires every rank's flag itself (all already set), so its
-  // peer loads are ordered after each peer's release.
-  for (int r = 0; r < p.world; ++r) (void)ld_acquire_sys(p.flags[p.rank] + (i64)r * p.nblocks + blockIdx.x);
-
-  // 3. Rank-order sums of this block's chunks, one chunk per warp at a time.
-  for (i64 ch = blockIdx.x + (i64)warp * gridDim.x; ch < nchunks; ch += (i64)kPeerWarps * gridDim.x) {
-    const i64 e = ch * 32 + lane;
-    if (e >= n) continue;
-    float t = 0.f;
-    for (int r = 0; r < p.world; ++r) t += __ldcv(p.bufs[r] + parity_off + e);
+    if (__any_sync(kFull, active && !ok) && lane == 0) atomicAdd(&g_peer_timeouts, 1u);
+    if (!active || !ok) continue;  // a timed-out output stays unwritten
     const i64 c = e / (W + 1);
     const int k = (int)(e - c * (W + 1));
     if (k < W) {
@@ -124,6 +117,10 @@ __global__ void __launch_bounds__(kPeerWarps * 32) finalize_peer_kernel(const Pe
       if (a.db_out && a.has_bias) static_cast<T*>(a.db_out)[c * a.dbs] = Cvt<T>::to(t);
     }
   }
+  // Advance the call number (every thread read it above).  Counted even
+  // after a timeout, so this rank's call numbers keep matching its peers'.
+  __syncthreads();
+  if (threadIdx.x == 0) *ep = epoch;
 }
 
 struct LaunchPeer {
@@ -141,6 +138,10 @@ struct LaunchPeer {
 i64 peer_blocks(i64 dim, int width) {
   const i64 chunks = ceil_div(dim * (width + 1), (i64)32);
   return chunks < kPeerMaxBlocks ? chunks : kPeerMaxBlocks;
+}
+
+i64 peer_exchange_bytes(i64 dim, int width, int world) {
+  return 2 * (i64)world * dim * (width + 1) * (i64)sizeof(unsigned long long);
 }
 
 cudaError_t launch_finalize_peer(int dtype, int width, const PeerFinalizeArgs& p, cudaStream_t stream) {

@@ -133,25 +133,27 @@ CC1D_API int cc1d_bwd(const cc1d_bwd_params* params, void* stream);
  * stream order) every rank's dwdb_acc / dweight_out / dbias_out hold the
  * sums over all ranks' batch shards -- bitwise identical on all ranks,
  * added in rank order.  Replaces the NCCL all-reduce of the fp32 buffer that
- * the reference's batch-sharded use would need (it has no multi-GPU code).
+ * a batch-sharded use of the reference's causal_conv1d_fn would need (the
+ * reference has no multi-GPU code).
  *
- * exchange[r] / flags[r]: rank r's buffers, mapped into this process (e.g.
- * symmetric memory); exchange holds 2*dim*(W+1) floats, flags
- * world*cc1d_peer_blocks(dim, W) uint32 and must be zero before the first
- * call.  epochs: this rank's cc1d_peer_blocks(dim, W) uint32 counters, zero
- * before the first call, advanced on the device by every call (so the call
- * may be captured in a CUDA graph).  All ranks must issue the same sequence
- * of calls with the same dim and W.  Waits for peers are bounded; a wait
- * that gives up is counted by cc1d_device_status.
+ * exchange[r]: rank r's exchange buffer, mapped into this process (e.g. by
+ * CUDA IPC), cc1d_peer_exchange_bytes(dim, W, world) bytes, zero before the
+ * first call; every rank stores into every other rank's buffer.  epochs:
+ * this rank's cc1d_peer_blocks(dim, W) uint32 call counters, zero before
+ * the first call, advanced on the device by every call (so the call may be
+ * captured in a CUDA graph and replayed).  All ranks must issue the same
+ * sequence of calls with the same dim and W, one rank per GPU.  Waits for
+ * peers are bounded; a wait that gives up leaves its outputs unwritten and
+ * is counted by cc1d_device_status.
  */
 typedef struct cc1d_peer_reduce {
-  int32_t rank, world;          /* world <= 32 */
-  float* const* exchange;       /* device array [world] */
-  uint32_t* const* flags;       /* device array [world] */
-  uint32_t* epochs;             /* this rank's counters */
+  int32_t rank, world;                 /* world <= 32 */
+  unsigned long long* const* exchange; /* device array [world] */
+  uint32_t* epochs;                    /* this rank's counters */
 } cc1d_peer_reduce;
 
 CC1D_API int64_t cc1d_peer_blocks(int64_t dim, int32_t width);
+CC1D_API int64_t cc1d_peer_exchange_bytes(int64_t dim, int32_t width, int32_t world);
 CC1D_API int cc1d_bwd_peer_reduce(const cc1d_bwd_params* params, const cc1d_peer_reduce* peer, void* stream);
 
 /*

@@ -33,7 +33,7 @@ REPO = Path(__file__).resolve().parent.parent
 
 pytestmark = pytest.mark.gpu
 
-WORLD = min(torch.cuda.device_count(), 4) if torch.cuda.is_available() else 0
+WORLD = min(torch.cuda.device_count(), 8) if torch.cuda.is_available() else 0
 
 
 def _free_port():
