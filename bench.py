@@ -5,14 +5,17 @@ prefill, causal_conv1d_fn forward + backward, bf16, x (8, 5376, 2048) in
 channel-last strides, width 4, bias, SiLU, initial_states and
 return_final_states, grad_out ~ N(0,1).  One step = forward + backward of
 one batch; with N GPUs every rank runs its own batch of 8 (global batch 8N,
-weak scaling) and the fp32 [dweight | dbias] partials are summed with one
-NCCL all-reduce.
+weak scaling) and the fp32 [dweight | dbias] partials are summed across the
+ranks inside the backward's reduction kernel (NVLink peer memory).
 
   value  -- whole-job tokens/s on device-resident inputs (CUDA events, max
             over ranks); inputs (176 MB per tensor) are larger than L2.
   e2e    -- the same step through the public API from pinned HOST buffers:
             host->device copies of the step's inputs and device->host reads
-            of all its outputs inside the timed region.
+            of all its outputs inside the timed region, issued as a serving
+            or training loop would: copy-in, compute and copy-out on three
+            streams, device inputs double-buffered, so step i+1's upload
+            overlaps step i's compute and download.
   roofline / kernels -- algorithmic HBM bytes / CUDA-event kernel time per
             op (fwd, bwd, decode update C3a/C3b, varlen C4, large C5) against
             the measured copy bandwidth of MEASURED_PEAKS.json.
@@ -273,7 +276,8 @@ def time_c2(args, world, rank, reducer):
 
 
 def time_e2e(args, world, rank, reducer):
-    """Public API, host buffers in and out, every step."""
+    """Public API, host buffers in and out, every step (three-stream
+    pipeline: upload of step i+1 and download of step i overlap compute)."""
     from causal_conv1d_b200 import causal_conv1d_fn
     from causal_conv1d_b200.parallel import causal_conv1d_fn_batch_sharded
 
@@ -286,39 +290,59 @@ def time_e2e(args, world, rank, reducer):
         out=(B, L, D), fs=(B, D, W - 1), dx=(B, L, D), dw=(D, W), db=(D,), dinit=(B, D, W - 1)).items()}
     h2d = sum(t.numel() * t.element_size() for t in host.values())
     d2h = sum(t.numel() * t.element_size() for t in outs.values())
+    dev_in = [{k: torch.empty_like(v, device="cuda") for k, v in host.items()} for _ in range(2)]
+    s_comp = torch.cuda.current_stream()
+    s_in, s_out = torch.cuda.Stream(), torch.cuda.Stream()
+    in_ready = [torch.cuda.Event() for _ in range(2)]
+    in_free = [torch.cuda.Event() for _ in range(2)]
+    for ev in in_free:
+        ev.record(s_comp)
 
-    def step():
-        x = host["x"].to("cuda", non_blocking=True).transpose(1, 2).requires_grad_()
-        w = host["w"].to("cuda", non_blocking=True).requires_grad_()
-        b = host["b"].to("cuda", non_blocking=True).requires_grad_()
-        init = host["init"].to("cuda", non_blocking=True).requires_grad_()
-        dout = host["dout"].to("cuda", non_blocking=True).transpose(1, 2)
+    def step(i):
+        k = i % 2
+        buf = dev_in[k]
+        with torch.cuda.stream(s_in):
+            s_in.wait_event(in_free[k])  # compute of step i-2 is done with this buffer set
+            for name, t in host.items():
+                buf[name].copy_(t, non_blocking=True)
+            in_ready[k].record(s_in)
+        s_comp.wait_event(in_ready[k])
+        x = buf["x"].transpose(1, 2).detach().requires_grad_()
+        w = buf["w"].detach().requires_grad_()
+        b = buf["b"].detach().requires_grad_()
+        init = buf["init"].detach().requires_grad_()
+        dout = buf["dout"].transpose(1, 2)
         if world > 1:
             out, fs = causal_conv1d_fn_batch_sharded(x, w, b, initial_states=init, return_final_states=True,
                                                       activation="silu", reducer=reducer)
         else:
             out, fs = causal_conv1d_fn(x, w, b, initial_states=init, return_final_states=True, activation="silu")
         torch.autograd.backward([out], [dout])
-        outs["out"].copy_(out.detach().transpose(1, 2), non_blocking=True)
-        outs["fs"].copy_(fs.detach(), non_blocking=True)
-        outs["dx"].copy_(x.grad.transpose(1, 2), non_blocking=True)
-        outs["dw"].copy_(w.grad, non_blocking=True)
-        outs["db"].copy_(b.grad, non_blocking=True)
-        outs["dinit"].copy_(init.grad, non_blocking=True)
+        in_free[k].record(s_comp)
+        results = dict(out=out.detach().transpose(1, 2), fs=fs.detach(), dx=x.grad.transpose(1, 2), dw=w.grad,
+                       db=b.grad, dinit=init.grad)
+        s_out.wait_stream(s_comp)
+        with torch.cuda.stream(s_out):
+            for name, t in results.items():
+                outs[name].copy_(t, non_blocking=True)
+                t.record_stream(s_out)  # keep the allocator off it until the download is done
 
     K = max(3, min(args.steps, 20))
-    for _ in range(max(3, args.warmup)):
-        step()
+    for i in range(max(3, args.warmup)):
+        step(i)
+    torch.cuda.synchronize()
     barrier_sync(world)
     start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    start.record()
-    for _ in range(K):
-        step()
-    stop.record()
+    start.record(s_in)
+    for i in range(K):
+        step(i)
+    stop.record(s_out)
     torch.cuda.synchronize()
     ms = max_over_ranks(start.elapsed_time(stop), world) / K
     return dict(value=world * B * L / (ms / 1e3), unit=UNIT, h2d_bytes_per_step=h2d, d2h_bytes_per_step=d2h,
-                ms_per_step=ms, steps=K, path="causal_conv1d_fn + autograd backward, pinned host buffers")
+                ms_per_step=ms, steps=K,
+                path="causal_conv1d_fn + autograd backward from pinned host buffers; upload, compute and download "
+                     "on three streams (device inputs double-buffered)")
 
 
 def _kernel_ms(fn, iters, sets):
