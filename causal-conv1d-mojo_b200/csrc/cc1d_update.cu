@@ -270,6 +270,118 @@ __global__ void __launch_bounds__(128) update_circ_kernel(const UpdateArgs a) {
   }
 }
 
+// A 16-bit or 32-bit element, given its bits in the low bits of `h`.
+template <typename T>
+__device__ __forceinline__ float bits_to_float(uint32_t h);
+template <>
+__device__ __forceinline__ float bits_to_float<float>(uint32_t h) { return __uint_as_float(h); }
+template <>
+__device__ __forceinline__ float bits_to_float<__nv_bfloat16>(uint32_t h) { return __uint_as_float(h << 16); }
+template <>
+__device__ __forceinline__ float bits_to_float<__half>(uint32_t h) {
+  return __half2float(__ushort_as_half((unsigned short)h));
+}
+
+// Element `i` of a state row held in NW 32-bit words (selects, no local
+// memory; the word predicates depend only on i, so they are shared by all
+// channels of a thread).
+template <typename T, int NW>
+__device__ __forceinline__ float row_elem(const uint32_t (&w)[NW], int i) {
+  const int wi = (i * (int)sizeof(T)) >> 2;
+  uint32_t word = w[0];
+#pragma unroll
+  for (int k = 1; k < NW; ++k) word = wi == k ? w[k] : word;
+  if (sizeof(T) == 4) return bits_to_float<T>(word);
+  return bits_to_float<T>((i & 1) ? (word >> 16) : (word & 0xffffu));
+}
+
+// Circular-buffer decode step (seqlen 1, cache_seqlens given) for state rows
+// of 16 or 32 bytes with unit element stride.  Each channel's whole row is
+// fetched with one or two 16-byte loads that do not wait for the buffer
+// position (nor for anything but the pool index), so the position load, the
+// rows, x, weight and bias are all in flight together -- one memory round
+// trip instead of two.  The W-1 window is then picked from registers.  A
+// warp's load covers 32 consecutive channel rows (512 or 1024 contiguous
+// bytes).  Same arithmetic order as update_circ_kernel.
+template <typename T, int W, int NW>
+__global__ void __launch_bounds__(128) update_circ_row_kernel(const UpdateArgs a) {
+  constexpr int H = W - 1;
+  constexpr int V = NW == 4 ? 8 : 4;  // channels per thread
+  constexpr int CHUNK = 128 * V;      // channels per block
+  const i64 chunks = ceil_div(a.D, (i64)CHUNK);
+  const i64 b = blockIdx.x / chunks;
+  const i64 cbase = (blockIdx.x - b * chunks) * CHUNK + (threadIdx.x >> 5) * (32 * V) + (threadIdx.x & 31);
+  const T* __restrict__ x = static_cast<const T*>(a.x);
+  const T* __restrict__ wt = static_cast<const T*>(a.w);
+  const T* __restrict__ bias = static_cast<const T*>(a.bias);
+  T* __restrict__ out = static_cast<T*>(a.out);
+  i64 row = b;
+  if (a.idx != nullptr) {
+    const int r = a.idx[b];
+    if (r < 0 || r >= a.state_rows) {
+#pragma unroll
+      for (int v = 0; v < V; ++v) {
+        const i64 c = cbase + 32 * v;
+        if (c < a.D) out[b * a.os_b + c * a.os_c] = Cvt<T>::to(0.f);
+      }
+      return;
+    }
+    row = r;
+  }
+  T* __restrict__ st = static_cast<T*>(a.state) + row * a.ss_b;
+  const int cs_raw = a.cache_seqlens[b];
+  uint32_t rw[V][NW];
+  T xv[V];
+  float acc[V];
+#pragma unroll
+  for (int v = 0; v < V; ++v) {
+    const i64 c = cbase + 32 * v;
+    acc[v] = 0.f;
+    xv[v] = Cvt<T>::to(0.f);
+#pragma unroll
+    for (int k = 0; k < NW; ++k) rw[v][k] = 0u;
+    if (c < a.D) {
+      const uint4* src = reinterpret_cast<const uint4*>(st + c * a.ss_c);
+#pragma unroll
+      for (int q = 0; q < NW / 4; ++q) {
+        const uint4 u = src[q];
+        rw[v][4 * q + 0] = u.x;
+        rw[v][4 * q + 1] = u.y;
+        rw[v][4 * q + 2] = u.z;
+        rw[v][4 * q + 3] = u.w;
+      }
+      xv[v] = x[b * a.xs_b + c * a.xs_c];
+      acc[v] = bias ? Cvt<T>::f(bias[c * a.bs]) : 0.f;
+    }
+  }
+  i64 cs = (i64)cs_raw % a.S;
+  if (cs < 0) cs += a.S;
+  int pos[H];
+  {
+    i64 ui = cs - H;
+    if (ui < 0) ui += a.S;
+#pragma unroll
+    for (int j = 0; j < H; ++j) {
+      pos[j] = (int)ui;
+      ui = (ui + 1 == a.S) ? 0 : ui + 1;
+    }
+  }
+#pragma unroll
+  for (int v = 0; v < V; ++v) {
+    const i64 c = cbase + 32 * v;
+    if (c < a.D) {
+#pragma unroll
+      for (int k = 0; k < H; ++k)
+        acc[v] = fmaf(Cvt<T>::f(wt[c * a.ws_c + k * a.ws_k]), row_elem<T, NW>(rw[v], pos[k]), acc[v]);
+      acc[v] = fmaf(Cvt<T>::f(wt[c * a.ws_c + H * a.ws_k]), Cvt<T>::f(xv[v]), acc[v]);
+      float o = acc[v];
+      if (a.silu) o = silu_f(o);
+      out[b * a.os_b + c * a.os_c] = Cvt<T>::to(o);
+      st[c * a.ss_c + cs] = xv[v];
+    }
+  }
+}
+
 template <typename T>
 __global__ void varlen_states_kernel(const VarlenArgs a) {
   const i64 n = a.B * a.S * a.D;
@@ -319,6 +431,18 @@ bool vec_path_ok(const UpdateArgs& a) {
          (a.bias == nullptr || (a.bs == 1 && aligned16(a.bias)));
 }
 
+// Circular rows of 16 or 32 bytes, unit element stride, 16-byte aligned:
+// returns the row size in 32-bit words (4 or 8), else 0.
+template <typename T>
+int circ_row_words(const UpdateArgs& a) {
+  if (a.cache_seqlens == nullptr || a.L != 1 || a.ss_l != 1 || !aligned16(a.state)) return 0;
+  const i64 esz = (i64)sizeof(T);
+  const i64 row_bytes = a.S * esz;
+  if (row_bytes != 16 && row_bytes != 32) return 0;
+  if ((a.ss_c * esz) % 16 != 0 || (a.ss_b * esz) % 16 != 0) return 0;
+  return (int)(row_bytes / 4);
+}
+
 struct LaunchUpdate {
   const UpdateArgs& a;
   cudaStream_t stream;
@@ -329,6 +453,19 @@ struct LaunchUpdate {
       const i64 blocks = ceil_div(a.D / 8, (i64)threads) * a.B;
       if (blocks > 0x7fffffffLL) return cudaErrorInvalidConfiguration;
       update_vec_kernel<T, W><<<(unsigned)blocks, threads, 0, stream>>>(a);
+      return cudaGetLastError();
+    }
+    const int nw = circ_row_words<T>(a);
+    if (nw == 4) {
+      const i64 blocks = ceil_div(a.D, (i64)threads * 8) * a.B;
+      if (blocks > 0x7fffffffLL) return cudaErrorInvalidConfiguration;
+      update_circ_row_kernel<T, W, 4><<<(unsigned)blocks, threads, 0, stream>>>(a);
+      return cudaGetLastError();
+    }
+    if (nw == 8) {
+      const i64 blocks = ceil_div(a.D, (i64)threads * 4) * a.B;
+      if (blocks > 0x7fffffffLL) return cudaErrorInvalidConfiguration;
+      update_circ_row_kernel<T, W, 8><<<(unsigned)blocks, threads, 0, stream>>>(a);
       return cudaGetLastError();
     }
     if (a.cache_seqlens != nullptr && a.L == 1) {

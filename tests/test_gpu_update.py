@@ -90,14 +90,16 @@ def test_decode_loop_matches_full_forward(dtype):
     assert torch.equal(full, dec)
 
 
+@pytest.mark.parametrize("row_bytes", [0, 16, 32])  # 0: state_len W-1; 16/32: whole-row kernel
 @pytest.mark.parametrize("dtype", ["fp32", "bf16"])
-def test_circular_decode_loop(dtype):
+def test_circular_decode_loop(dtype, row_bytes):
     dt = DTYPES[dtype]
     B, D, L, W = 1, 8, 16, 4
+    S = W - 1 if row_bytes == 0 else row_bytes // torch.tensor([], dtype=dt).element_size()
     x = torch.randn(B, D, L, dtype=dt, device=DEV)
     w = torch.randn(D, W, dtype=dt, device=DEV)
     full = causal_conv1d_fn(x, w, activation="silu")
-    state = torch.zeros(B, D, W - 1, dtype=dt, device=DEV)
+    state = torch.zeros(B, D, S, dtype=dt, device=DEV)
     outs = []
     for t in range(L):
         cs = torch.tensor([t], dtype=torch.int32, device=DEV)
@@ -157,28 +159,44 @@ def test_varlen_random_vs_ref(dtype):
         assert_bitwise(got, oracle.varlen_states(x, cu, S), f"S={S} (oracle)")
 
 
+@pytest.mark.parametrize("D", [1024, 1000])
+@pytest.mark.parametrize("row_bytes", [16, 32])
 @pytest.mark.parametrize("pool", [False, True])
 @pytest.mark.parametrize("dtype,W", [("bf16", 2), ("bf16", 4), ("bf16", 9), ("fp16", 5), ("fp32", 2), ("fp32", 5)])
-def test_circular_serving_state_len_vs_oracle(dtype, W, pool):
-    """Circular decode with the serving state_len (8 for 16-bit types, 4 for
-    fp32), full write-head range incl. negative and wrapped values."""
+def test_circular_serving_state_len_vs_oracle(dtype, W, pool, row_bytes, D):
+    """Circular decode with the serving state lengths (rows of 16 or 32 bytes:
+    8 / 16 elements for 16-bit types, 4 / 8 for fp32) -- the whole-row kernel
+    -- over the full write-head range incl. negative and wrapped values; a
+    ragged dim; pool rows at a channel pitch of twice the row (a dim slice)."""
     dt = DTYPES[dtype]
-    S = 16 // torch.tensor([], dtype=dt).element_size()
-    B, D = 7, 1024
+    S = row_bytes // torch.tensor([], dtype=dt).element_size()
+    if W - 1 > S:
+        pytest.skip("state shorter than the window")
+    B = 7
     rows = 2 * B if pool else B
     x = seeded((B, D), dt, W)
     w = seeded((D, W), dt, W + 1, "uniform")
     b = seeded((D,), dt, W + 2, "uniform")
     state = seeded((rows, D, S), dt, W + 3)
+    if pool:
+        big = torch.zeros(rows, 2 * D, S, dtype=dt)
+        big[:, ::2] = state
+        state = big[:, ::2]
     cache = torch.tensor([0, 1, S - 1, S, 1023, -1, -S - 3], dtype=torch.int32)
     idx = None
     if pool:
         idx = torch.randperm(rows, generator=torch.Generator().manual_seed(W))[:B].to(torch.int32)
         idx[2] = -1
-    st_g = state.to(DEV)
+    if pool:
+        big_g = big.to(DEV)
+        st_g = big_g[:, ::2]
+    else:
+        st_g = state.to(DEV)
     out = causal_conv1d_update(x.to(DEV), st_g, w.to(DEV), b.to(DEV), activation="silu", cache_seqlens=cache.to(DEV),
                                conv_state_indices=idx.to(DEV) if idx is not None else None)
     st_o = state.clone()
     o = oracle.update(x, st_o, w, b, silu=True, cache_seqlens=cache, conv_state_indices=idx)
     assert_close(out.cpu(), o, dt, "out")
     assert_bitwise(st_g.cpu(), st_o, "conv_state")
+    if pool:
+        assert torch.count_nonzero(big_g[:, 1::2]) == 0  # the interleaved rows are never written
