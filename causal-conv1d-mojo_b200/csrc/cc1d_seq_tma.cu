@@ -31,9 +31,32 @@ namespace cc1d {
 
 namespace {
 
-constexpr int kSW = 4;              // consumer warps
-constexpr int kRows = 2 * kSW;      // channel rows per tile
-constexpr int kTL = 256;            // positions per tile (32 lanes x 8)
+// Tunables (measured on B200; overridable at build time for sweeps).
+#ifndef CC1D_SEQ_WARPS
+#define CC1D_SEQ_WARPS 4        // consumer warps per block
+#endif
+#ifndef CC1D_SEQ_FWD_STAGES16
+#define CC1D_SEQ_FWD_STAGES16 8  // forward ring stages, 16-bit types
+#endif
+#ifndef CC1D_SEQ_FWD_STAGES32
+#define CC1D_SEQ_FWD_STAGES32 4  // forward ring stages, fp32
+#endif
+#ifndef CC1D_SEQ_BWD_STAGES16
+#define CC1D_SEQ_BWD_STAGES16 4  // backward ring stages (x + dout tiles), 16-bit types
+#endif
+#ifndef CC1D_SEQ_BWD_STAGES32
+#define CC1D_SEQ_BWD_STAGES32 3  // backward ring stages, fp32
+#endif
+#ifndef CC1D_SEQ_FWD_MIN_BLOCKS
+#define CC1D_SEQ_FWD_MIN_BLOCKS 1
+#endif
+#ifndef CC1D_SEQ_BWD_MIN_BLOCKS
+#define CC1D_SEQ_BWD_MIN_BLOCKS 4  // widths <= 5: registers capped at 96, 4 blocks per SM (3 without: -16% at C5)
+#endif
+
+constexpr int kSW = CC1D_SEQ_WARPS;  // consumer warps
+constexpr int kRows = 2 * kSW;       // channel rows per tile
+constexpr int kTL = 256;             // positions per tile (32 lanes x 8)
 constexpr int kThreadsSeq = (kSW + 1) * 32;
 
 template <typename T>
@@ -42,11 +65,11 @@ constexpr unsigned seq_tile_bytes() {
 }
 template <typename T>
 constexpr int seq_fwd_stages() {
-  return 32768 / seq_tile_bytes<T>();  // 16-bit: 8, fp32: 4
+  return sizeof(T) == 2 ? CC1D_SEQ_FWD_STAGES16 : CC1D_SEQ_FWD_STAGES32;
 }
 template <typename T>
 constexpr int seq_bwd_stages() {
-  return 49152 / (2 * seq_tile_bytes<T>());  // 16-bit: 6, fp32: 3
+  return sizeof(T) == 2 ? CC1D_SEQ_BWD_STAGES16 : CC1D_SEQ_BWD_STAGES32;
 }
 
 struct alignas(64) SeqFwdParams {
@@ -128,7 +151,7 @@ __device__ __forceinline__ float2 xc_pair(const T* x, i64 xs_c, i64 xs_l, const 
 // ---------------------------------------------------------------------------
 
 template <typename T, int W, bool SILU>
-__global__ void __launch_bounds__(kThreadsSeq) fwd_seq_tma_kernel(const __grid_constant__ SeqFwdParams p) {
+__global__ void __launch_bounds__(kThreadsSeq, CC1D_SEQ_FWD_MIN_BLOCKS) fwd_seq_tma_kernel(const __grid_constant__ SeqFwdParams p) {
   constexpr int H = W - 1;
   constexpr unsigned TB = seq_tile_bytes<T>();
   constexpr int NS = seq_fwd_stages<T>();
@@ -271,7 +294,7 @@ __device__ __forceinline__ void emit_dx(const float2 (&d)[8], const float2 (&rh)
 }
 
 template <typename T, int W, bool SILU>
-__global__ void __launch_bounds__(kThreadsSeq) bwd_seq_tma_kernel(const __grid_constant__ SeqBwdParams p) {
+__global__ void __launch_bounds__(kThreadsSeq, W <= 5 ? CC1D_SEQ_BWD_MIN_BLOCKS : 1) bwd_seq_tma_kernel(const __grid_constant__ SeqBwdParams p) {
   constexpr int H = W - 1;
   constexpr unsigned TB = seq_tile_bytes<T>();
   constexpr unsigned SB = 2 * TB;
