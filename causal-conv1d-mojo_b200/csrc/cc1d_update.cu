@@ -295,53 +295,90 @@ __device__ __forceinline__ float row_elem(const uint32_t (&w)[NW], int i) {
   return bits_to_float<T>((i & 1) ? (word >> 16) : (word & 0xffffu));
 }
 
+// W weights of one channel as floats: one vector load when they are
+// contiguous and the vector is 4, 8 or 16 bytes, else W scalar loads.
+template <typename T, int W>
+__device__ __forceinline__ void load_taps(const T* __restrict__ p, i64 ws_k, bool vec, float (&w)[W]) {
+  constexpr int BYTES = W * (int)sizeof(T);
+  if constexpr (BYTES == 4 || BYTES == 8 || BYTES == 16) {
+    if (vec) {
+      const Pack<T, W> pk = ld_pack<T, W>(p);
+#pragma unroll
+      for (int k = 0; k < W; ++k) w[k] = Cvt<T>::f(pk.v[k]);
+      return;
+    }
+  }
+#pragma unroll
+  for (int k = 0; k < W; ++k) w[k] = Cvt<T>::f(p[k * ws_k]);
+}
+
 // Circular-buffer decode step (seqlen 1, cache_seqlens given) for state rows
 // of 16 or 32 bytes with unit element stride.  Each channel's whole row is
 // fetched with one or two 16-byte loads that do not wait for the buffer
 // position (nor for anything but the pool index), so the position load, the
 // rows, x, weight and bias are all in flight together -- one memory round
-// trip instead of two.  The W-1 window is then picked from registers.  A
-// warp's load covers 32 consecutive channel rows (512 or 1024 contiguous
-// bytes).  Same arithmetic order as update_circ_kernel.
+// trip instead of two.  The W-1 window is then picked from registers.
+// Warps are mapped flat onto (batch row, range of 32*V channels), lane l
+// taking channels l, l+32, ..., so a warp's row load covers 32 consecutive
+// channel rows (512 or 1024 contiguous bytes) and no warp straddles two
+// batch rows.  Addresses advance by precomputed pointer steps.  Same
+// arithmetic order as update_circ_kernel.
+// Few channels per lane and a full SM of warps beat deep per-thread batches
+// here (B200, C3b shape: 2 / 16 -> 12.5 us; 8 / none -> 22.7 us): the
+// kernel is bound by memory latency, not by instruction count.
+#ifndef CC1D_CIRC_V16
+#define CC1D_CIRC_V16 2  // channels per lane for 16-byte rows (half that for 32-byte rows)
+#endif
+#ifndef CC1D_CIRC_MIN_BLOCKS
+#define CC1D_CIRC_MIN_BLOCKS 16
+#endif
+template <int NW>
+constexpr int circ_lane_channels() {
+  return NW == 4 ? CC1D_CIRC_V16 : (CC1D_CIRC_V16 / 2 > 0 ? CC1D_CIRC_V16 / 2 : 1);
+}
+
 template <typename T, int W, int NW>
-__global__ void __launch_bounds__(128) update_circ_row_kernel(const UpdateArgs a) {
+__global__ void __launch_bounds__(128, CC1D_CIRC_MIN_BLOCKS) update_circ_row_kernel(const UpdateArgs a,
+                                                                                   const i64 warps_per_row,
+                                                                                   const bool taps_vec) {
   constexpr int H = W - 1;
-  constexpr int V = NW == 4 ? 8 : 4;  // channels per thread
-  constexpr int CHUNK = 128 * V;      // channels per block
-  const i64 chunks = ceil_div(a.D, (i64)CHUNK);
-  const i64 b = blockIdx.x / chunks;
-  const i64 cbase = (blockIdx.x - b * chunks) * CHUNK + (threadIdx.x >> 5) * (32 * V) + (threadIdx.x & 31);
-  const T* __restrict__ x = static_cast<const T*>(a.x);
-  const T* __restrict__ wt = static_cast<const T*>(a.w);
-  const T* __restrict__ bias = static_cast<const T*>(a.bias);
-  T* __restrict__ out = static_cast<T*>(a.out);
+  constexpr int V = circ_lane_channels<NW>();  // channels per lane
+  const i64 gw = ((i64)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const i64 b = gw / warps_per_row;
+  if (b >= a.B) return;
+  const int lane = threadIdx.x & 31;
+  const i64 c0 = (gw - b * warps_per_row) * (32 * V) + lane;
+  const int nv = c0 >= a.D ? 0 : (int)min((i64)V, (a.D - c0 + 31) >> 5);  // channels of this lane in range
+  T* __restrict__ out = static_cast<T*>(a.out) + b * a.os_b + c0 * a.os_c;
+  const i64 out_step = 32 * a.os_c;
   i64 row = b;
   if (a.idx != nullptr) {
     const int r = a.idx[b];
     if (r < 0 || r >= a.state_rows) {
 #pragma unroll
-      for (int v = 0; v < V; ++v) {
-        const i64 c = cbase + 32 * v;
-        if (c < a.D) out[b * a.os_b + c * a.os_c] = Cvt<T>::to(0.f);
-      }
+      for (int v = 0; v < V; ++v)
+        if (v < nv) out[v * out_step] = Cvt<T>::to(0.f);
       return;
     }
     row = r;
   }
-  T* __restrict__ st = static_cast<T*>(a.state) + row * a.ss_b;
+  T* __restrict__ st = static_cast<T*>(a.state) + row * a.ss_b + c0 * a.ss_c;
+  const i64 st_step = 32 * a.ss_c;
+  const T* __restrict__ xp = static_cast<const T*>(a.x) + b * a.xs_b + c0 * a.xs_c;
+  const i64 x_step = 32 * a.xs_c;
+  const T* __restrict__ wp = static_cast<const T*>(a.w) + c0 * a.ws_c;
+  const i64 w_step = 32 * a.ws_c;
+  const T* __restrict__ bp = a.bias ? static_cast<const T*>(a.bias) + c0 * a.bs : nullptr;
+  const i64 b_step = 32 * a.bs;
   const int cs_raw = a.cache_seqlens[b];
   uint32_t rw[V][NW];
   T xv[V];
+  float wv[V][W];
   float acc[V];
 #pragma unroll
   for (int v = 0; v < V; ++v) {
-    const i64 c = cbase + 32 * v;
-    acc[v] = 0.f;
-    xv[v] = Cvt<T>::to(0.f);
-#pragma unroll
-    for (int k = 0; k < NW; ++k) rw[v][k] = 0u;
-    if (c < a.D) {
-      const uint4* src = reinterpret_cast<const uint4*>(st + c * a.ss_c);
+    if (v < nv) {
+      const uint4* src = reinterpret_cast<const uint4*>(st + v * st_step);
 #pragma unroll
       for (int q = 0; q < NW / 4; ++q) {
         const uint4 u = src[q];
@@ -350,34 +387,33 @@ __global__ void __launch_bounds__(128) update_circ_row_kernel(const UpdateArgs a
         rw[v][4 * q + 2] = u.z;
         rw[v][4 * q + 3] = u.w;
       }
-      xv[v] = x[b * a.xs_b + c * a.xs_c];
-      acc[v] = bias ? Cvt<T>::f(bias[c * a.bs]) : 0.f;
+      xv[v] = xp[v * x_step];
+      load_taps<T, W>(wp + v * w_step, a.ws_k, taps_vec, wv[v]);
+      acc[v] = bp ? Cvt<T>::f(bp[v * b_step]) : 0.f;
     }
   }
-  i64 cs = (i64)cs_raw % a.S;
-  if (cs < 0) cs += a.S;
+  int cs = (int)((i64)cs_raw % a.S);
+  if (cs < 0) cs += (int)a.S;
   int pos[H];
   {
-    i64 ui = cs - H;
-    if (ui < 0) ui += a.S;
+    int ui = cs - H;
+    if (ui < 0) ui += (int)a.S;
 #pragma unroll
     for (int j = 0; j < H; ++j) {
-      pos[j] = (int)ui;
-      ui = (ui + 1 == a.S) ? 0 : ui + 1;
+      pos[j] = ui;
+      ui = (ui + 1 == (int)a.S) ? 0 : ui + 1;
     }
   }
 #pragma unroll
   for (int v = 0; v < V; ++v) {
-    const i64 c = cbase + 32 * v;
-    if (c < a.D) {
+    if (v < nv) {
 #pragma unroll
-      for (int k = 0; k < H; ++k)
-        acc[v] = fmaf(Cvt<T>::f(wt[c * a.ws_c + k * a.ws_k]), row_elem<T, NW>(rw[v], pos[k]), acc[v]);
-      acc[v] = fmaf(Cvt<T>::f(wt[c * a.ws_c + H * a.ws_k]), Cvt<T>::f(xv[v]), acc[v]);
+      for (int k = 0; k < H; ++k) acc[v] = fmaf(wv[v][k], row_elem<T, NW>(rw[v], pos[k]), acc[v]);
+      acc[v] = fmaf(wv[v][H], Cvt<T>::f(xv[v]), acc[v]);
       float o = acc[v];
       if (a.silu) o = silu_f(o);
-      out[b * a.os_b + c * a.os_c] = Cvt<T>::to(o);
-      st[c * a.ss_c + cs] = xv[v];
+      out[v * out_step] = Cvt<T>::to(o);
+      st[v * st_step + cs] = xv[v];
     }
   }
 }
@@ -456,16 +492,18 @@ struct LaunchUpdate {
       return cudaGetLastError();
     }
     const int nw = circ_row_words<T>(a);
-    if (nw == 4) {
-      const i64 blocks = ceil_div(a.D, (i64)threads * 8) * a.B;
+    if (nw == 4 || nw == 8) {
+      const int V = nw == 4 ? circ_lane_channels<4>() : circ_lane_channels<8>();
+      const i64 warps_per_row = ceil_div(a.D, (i64)32 * V);
+      const i64 blocks = ceil_div(a.B * warps_per_row, (i64)threads / 32);
       if (blocks > 0x7fffffffLL) return cudaErrorInvalidConfiguration;
-      update_circ_row_kernel<T, W, 4><<<(unsigned)blocks, threads, 0, stream>>>(a);
-      return cudaGetLastError();
-    }
-    if (nw == 8) {
-      const i64 blocks = ceil_div(a.D, (i64)threads * 4) * a.B;
-      if (blocks > 0x7fffffffLL) return cudaErrorInvalidConfiguration;
-      update_circ_row_kernel<T, W, 8><<<(unsigned)blocks, threads, 0, stream>>>(a);
+      const i64 tb = W * (i64)sizeof(T);
+      const bool taps_vec = a.ws_k == 1 && (tb == 4 || tb == 8 || tb == 16) && (a.ws_c * (i64)sizeof(T)) % tb == 0 &&
+                            (reinterpret_cast<uintptr_t>(a.w) % (uintptr_t)tb) == 0;
+      if (nw == 4)
+        update_circ_row_kernel<T, W, 4><<<(unsigned)blocks, threads, 0, stream>>>(a, warps_per_row, taps_vec);
+      else
+        update_circ_row_kernel<T, W, 8><<<(unsigned)blocks, threads, 0, stream>>>(a, warps_per_row, taps_vec);
       return cudaGetLastError();
     }
     if (a.cache_seqlens != nullptr && a.L == 1) {
