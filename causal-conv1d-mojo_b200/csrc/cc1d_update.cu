@@ -101,21 +101,45 @@ __global__ void __launch_bounds__(128) update_kernel(const UpdateArgs a) {
   }
 }
 
-// Fast path of the linear decode step for the common serving layout: one new
-// token (L == 1), conv_state rows contiguous (stride 1 over state_len, state_len
-// elements per channel), weights (D, W) contiguous, x/out with unit channel
-// stride, 16-byte aligned rows, D % 8 == 0.  A thread owns 8 adjacent channels
-// of one batch row: x, bias, the weights and (linear mode) the state rows are
-// read as 16-byte vectors, all before any store, so a block has two dependent
-// memory round trips (the pool index, then everything else) and the grid is
-// about half a wave at the serving shapes.
-// Linear mode with state_len == W-1: new state = [old[1..W-2], x].
+// Largest vector (in elements, a power of two, at most 16 bytes) that
+// divides a run of N contiguous elements of T.
+template <typename T, int N>
+constexpr int vec_elems() {
+  int e = 16 / (int)sizeof(T);
+  while (e > 1 && N % e != 0) e /= 2;
+  return e;
+}
+
+// Plain (coherent) vector load, for data this kernel also writes.
+template <typename T, int N>
+__device__ __forceinline__ Pack<T, N> ld_pack_rw(const T* p) {
+  Pack<T, N> pk;
+  pk.raw = *reinterpret_cast<const typename Pack<T, N>::Raw*>(p);
+  return pk;
+}
+
+// Channels per thread of the linear single-token update (B200, C3a shape:
+// 4 -> 6.45 us, 8 -> 7.13 us, 2 -> 7.0 us).
+#ifndef CC1D_VEC_V
+#define CC1D_VEC_V 4
+#endif
+#ifndef CC1D_VEC_MIN_BLOCKS
+#define CC1D_VEC_MIN_BLOCKS 1
+#endif
+constexpr int kVecV = CC1D_VEC_V;
+
+// Linear single-token update with V contiguous channels per thread: x, bias,
+// out are V-element runs, weights V*W, state V*(W-1) (state_len == W-1 and
+// rows packed, so a thread's state is one contiguous run); every run moves
+// as the widest aligned vectors that divide it.  All loads are independent
+// (only the state row waits for the pool index).
 template <typename T, int W>
-__global__ void __launch_bounds__(128) update_vec_kernel(const UpdateArgs a) {
+__global__ void __launch_bounds__(128, CC1D_VEC_MIN_BLOCKS) update_vec_kernel(const UpdateArgs a) {
   constexpr int H = W - 1;
-  constexpr int V = 8;  // channels per thread
-  typedef Pack<T, 16 / sizeof(T)> P16;
-  constexpr int E16 = 16 / sizeof(T);  // elements per 16-byte vector
+  constexpr int V = kVecV;
+  constexpr int EX = vec_elems<T, V>();
+  constexpr int EW = vec_elems<T, V * W>();
+  constexpr int ES = vec_elems<T, V * H>();
   const i64 groups = a.D / V;
   const i64 cblocks = ceil_div(groups, (i64)blockDim.x);
   const i64 b = blockIdx.x / cblocks;
@@ -127,49 +151,49 @@ __global__ void __launch_bounds__(128) update_vec_kernel(const UpdateArgs a) {
   if (a.idx != nullptr) {
     const int r = a.idx[b];
     if (r < 0 || r >= a.state_rows) {
-      P16 z;
+      Pack<T, EX> z;
 #pragma unroll
-      for (int i = 0; i < E16; ++i) z.v[i] = Cvt<T>::to(0.f);
+      for (int i = 0; i < EX; ++i) z.v[i] = Cvt<T>::to(0.f);
 #pragma unroll
-      for (int i = 0; i < V; i += E16) st_pack<T, E16>(ob + i, z);
+      for (int i = 0; i < V; i += EX) st_pack<T, EX>(ob + i, z);
       return;
     }
     row = r;
   }
   T* __restrict__ st = static_cast<T*>(a.state) + row * a.ss_b + c0 * a.S;
-  // Loads: x, bias, weights, state -- all independent.
   T xv[V], bv[V], wv[V * W], sv[V * H];
+  const T* __restrict__ xp = static_cast<const T*>(a.x) + b * a.xs_b + c0;
 #pragma unroll
-  for (int i = 0; i < V; i += E16) {
-    const P16 px = ld_pack<T, E16>(static_cast<const T*>(a.x) + b * a.xs_b + c0 + i);
+  for (int i = 0; i < V; i += EX) {
+    const Pack<T, EX> px = ld_pack<T, EX>(xp + i);
 #pragma unroll
-    for (int e = 0; e < E16; ++e) xv[i + e] = px.v[e];
+    for (int e = 0; e < EX; ++e) xv[i + e] = px.v[e];
   }
   if (a.bias != nullptr) {
 #pragma unroll
-    for (int i = 0; i < V; i += E16) {
-      const P16 pb = ld_pack<T, E16>(static_cast<const T*>(a.bias) + c0 + i);
+    for (int i = 0; i < V; i += EX) {
+      const Pack<T, EX> pb = ld_pack<T, EX>(static_cast<const T*>(a.bias) + c0 + i);
 #pragma unroll
-      for (int e = 0; e < E16; ++e) bv[i + e] = pb.v[e];
+      for (int e = 0; e < EX; ++e) bv[i + e] = pb.v[e];
     }
   } else {
 #pragma unroll
     for (int i = 0; i < V; ++i) bv[i] = Cvt<T>::to(0.f);
   }
 #pragma unroll
-  for (int i = 0; i < V * W; i += E16) {
-    const P16 pw = ld_pack<T, E16>(static_cast<const T*>(a.w) + c0 * W + i);
+  for (int i = 0; i < V * W; i += EW) {
+    const Pack<T, EW> pw = ld_pack<T, EW>(static_cast<const T*>(a.w) + c0 * W + i);
 #pragma unroll
-    for (int e = 0; e < E16; ++e) wv[i + e] = pw.v[e];
+    for (int e = 0; e < EW; ++e) wv[i + e] = pw.v[e];
   }
 #pragma unroll
-  for (int i = 0; i < V * H; i += E16) {
-    const P16 ps = ld_pack<T, E16>(st + i);
+  for (int i = 0; i < V * H; i += ES) {
+    const Pack<T, ES> ps = ld_pack_rw<T, ES>(st + i);
 #pragma unroll
-    for (int e = 0; e < E16; ++e) sv[i + e] = ps.v[e];
+    for (int e = 0; e < ES; ++e) sv[i + e] = ps.v[e];
   }
   // Compute (same tap order and SiLU as every other kernel).
-  P16 po[V / E16 > 0 ? V / E16 : 1];
+  Pack<T, EX> po[V / EX];
 #pragma unroll
   for (int v = 0; v < V; ++v) {
     float acc = Cvt<T>::f(bv[v]);
@@ -177,11 +201,10 @@ __global__ void __launch_bounds__(128) update_vec_kernel(const UpdateArgs a) {
     for (int k = 0; k < H; ++k) acc = fmaf(Cvt<T>::f(wv[v * W + k]), Cvt<T>::f(sv[v * H + k]), acc);
     acc = fmaf(Cvt<T>::f(wv[v * W + H]), Cvt<T>::f(xv[v]), acc);
     if (a.silu) acc = silu_f(acc);
-    po[v / E16].v[v % E16] = Cvt<T>::to(acc);
+    po[v / EX].v[v % EX] = Cvt<T>::to(acc);
   }
-  // Stores.
 #pragma unroll
-  for (int i = 0; i < V; i += E16) st_pack<T, E16>(ob + i, po[i / E16]);
+  for (int i = 0; i < V; i += EX) st_pack<T, EX>(ob + i, po[i / EX]);
   // New rows [old[1..H-1], x] for the V channels, packed back to vectors.
   T nv[V * H];
 #pragma unroll
@@ -191,11 +214,11 @@ __global__ void __launch_bounds__(128) update_vec_kernel(const UpdateArgs a) {
     nv[v * H + H - 1] = xv[v];
   }
 #pragma unroll
-  for (int i = 0; i < V * H; i += E16) {
-    P16 pn;
+  for (int i = 0; i < V * H; i += ES) {
+    Pack<T, ES> pn;
 #pragma unroll
-    for (int e = 0; e < E16; ++e) pn.v[e] = nv[i + e];
-    st_pack<T, E16>(st + i, pn);
+    for (int e = 0; e < ES; ++e) pn.v[e] = nv[i + e];
+    st_pack<T, ES>(st + i, pn);
   }
 }
 
@@ -456,15 +479,22 @@ cudaError_t dispatch_update_width(int width, F&& f) {
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
-// Conditions of update_vec_kernel (see its comment).
+bool aligned_bytes(const void* p, i64 bytes) { return (reinterpret_cast<uintptr_t>(p) % (uintptr_t)bytes) == 0; }
+
+// Conditions of update_vec_kernel: one new token, linear mode with
+// state_len == W-1 and packed rows, (D, W) contiguous weights, unit channel
+// stride for x / out / bias, D a multiple of the channels per thread, and
+// every run aligned to the vector that moves it.
 template <typename T, int W>
 bool vec_path_ok(const UpdateArgs& a) {
-  const i64 e = 16 / (i64)sizeof(T);  // elements per 16 bytes
-  return a.cache_seqlens == nullptr && a.L == 1 && a.D % 8 == 0 && a.S == W - 1 && a.ss_l == 1 && a.ss_c == a.S &&
-         aligned16(a.state) && (a.ss_b % e == 0) && ((8 * a.S) % e == 0) && a.ws_k == 1 && a.ws_c == W &&
-         aligned16(a.w) && (8 * W) % e == 0 && a.xs_c == 1 && aligned16(a.x) && (a.B == 1 || a.xs_b % e == 0) &&
-         a.os_c == 1 && aligned16(a.out) && (a.B == 1 || a.os_b % e == 0) &&
-         (a.bias == nullptr || (a.bs == 1 && aligned16(a.bias)));
+  constexpr int V = kVecV;
+  constexpr i64 esz = (i64)sizeof(T);
+  constexpr i64 EX = vec_elems<T, V>(), EW = vec_elems<T, V * W>(), ES = vec_elems<T, V * (W - 1)>();
+  return a.cache_seqlens == nullptr && a.L == 1 && a.D % V == 0 && a.S == W - 1 && a.ss_l == 1 && a.ss_c == a.S &&
+         aligned_bytes(a.state, ES * esz) && a.ss_b % ES == 0 && a.ws_k == 1 && a.ws_c == W &&
+         aligned_bytes(a.w, EW * esz) && a.xs_c == 1 && aligned_bytes(a.x, EX * esz) &&
+         (a.B == 1 || a.xs_b % EX == 0) && a.os_c == 1 && aligned_bytes(a.out, EX * esz) &&
+         (a.B == 1 || a.os_b % EX == 0) && (a.bias == nullptr || (a.bs == 1 && aligned_bytes(a.bias, EX * esz)));
 }
 
 // Circular rows of 16 or 32 bytes, unit element stride, 16-byte aligned:
@@ -486,7 +516,7 @@ struct LaunchUpdate {
   cudaError_t operator()() {
     const int threads = 128;
     if (vec_path_ok<T, W>(a)) {
-      const i64 blocks = ceil_div(a.D / 8, (i64)threads) * a.B;
+      const i64 blocks = ceil_div(a.D / kVecV, (i64)threads) * a.B;
       if (blocks > 0x7fffffffLL) return cudaErrorInvalidConfiguration;
       update_vec_kernel<T, W><<<(unsigned)blocks, threads, 0, stream>>>(a);
       return cudaGetLastError();
