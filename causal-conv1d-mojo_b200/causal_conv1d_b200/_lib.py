@@ -97,7 +97,8 @@ class VarlenParams(ctypes.Structure):
 
 
 class PeerReduceParams(ctypes.Structure):
-    _fields_ = [("rank", c_i32), ("world", c_i32), ("exchange", c_ptr), ("epochs", c_ptr)]
+    _fields_ = [("rank", c_i32), ("world", c_i32), ("exchange", c_ptr), ("epochs", c_ptr),
+                ("max_polls", ctypes.c_uint32), ("reserved", ctypes.c_uint32)]
 
 
 # Every symbol include/cc1d.h declares, with its ctypes signature.

@@ -222,6 +222,7 @@ def _bwd_peer_impl(
     epochs: torch.Tensor,
     rank: int,
     world: int,
+    max_polls: int = 0,
 ) -> None:
     """Backward of a batch shard with dweight/dbias summed over `world` ranks
     in the same kernel (cc1d_bwd_peer_reduce).  exchange_ptrs: int64 device
@@ -233,6 +234,7 @@ def _bwd_peer_impl(
     q = _lib.PeerReduceParams()
     q.rank, q.world = rank, world
     q.exchange, q.epochs = exchange_ptrs.data_ptr(), epochs.data_ptr()
+    q.max_polls = max_polls
     with _on_device(x.device):
         nbytes = bwd_workspace_bytes(p)
         ws = None
@@ -246,7 +248,7 @@ def _bwd_peer_impl(
 
 
 def _bwd_peer_fake(x, weight, bias, dout, initial_states, dfinal_states, dx, dwdb_acc, dinitial_states,
-                   dweight_out, dbias_out, apply_silu, exchange_ptrs, epochs, rank, world) -> None:
+                   dweight_out, dbias_out, apply_silu, exchange_ptrs, epochs, rank, world, max_polls=0) -> None:
     return None
 
 

@@ -297,7 +297,8 @@ int bwd_impl(const cc1d_bwd_params* p, const cc1d_peer_reduce* peer, void* strea
     e = launch_finalize(p->dtype, p->width, f, s);
     if (e != cudaSuccess) return cuda_fail(e, "cc1d_bwd finalize launch");
   } else {
-    PeerFinalizeArgs pf{f, peer->rank, peer->world, peer->exchange, peer->epochs, peer_blocks(p->dim, p->width)};
+    PeerFinalizeArgs pf{f, peer->rank, peer->world, peer->exchange, peer->epochs, peer_blocks(p->dim, p->width),
+                        peer->max_polls != 0 ? peer->max_polls : 4194304u};
     e = launch_finalize_peer(p->dtype, p->width, pf, s);
     if (e != cudaSuccess) return cuda_fail(e, "cc1d_bwd_peer_reduce finalize launch");
   }

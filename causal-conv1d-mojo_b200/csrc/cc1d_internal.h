@@ -79,6 +79,7 @@ struct PeerFinalizeArgs {
   unsigned long long* const* bufs;  // device array [world] of exchange buffers
   uint32_t* epochs;                 // this rank's per-block call counters (nblocks)
   i64 nblocks;
+  unsigned max_polls;               // bounded wait per peer word
 };
 
 struct UpdateArgs {

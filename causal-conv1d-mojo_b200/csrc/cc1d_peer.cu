@@ -34,7 +34,6 @@ namespace {
 
 constexpr int kPeerWarps = 8;
 constexpr i64 kPeerMaxBlocks = 1024;      // B200: 148 SMs x 8 blocks of 256 threads resident
-constexpr unsigned kPeerSpin = 1u << 22;  // polls per lane (with back-off) before giving up
 
 static __device__ unsigned int g_peer_timeouts = 0;
 
@@ -94,7 +93,7 @@ __global__ void __launch_bounds__(kPeerWarps * 32) finalize_peer_kernel(const Pe
       for (int r = 0; r < p.world && ok; ++r) {
         unsigned long long w = ld_relaxed_sys_u64(mine + (i64)r * n + e);
         while ((w & 0xffffffff00000000ull) != tag) {
-          if (++polls > kPeerSpin) {
+          if (++polls > p.max_polls) {
             ok = false;
             break;
           }

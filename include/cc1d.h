@@ -150,6 +150,8 @@ typedef struct cc1d_peer_reduce {
   int32_t rank, world;                 /* world <= 32 */
   unsigned long long* const* exchange; /* device array [world] */
   uint32_t* epochs;                    /* this rank's counters */
+  uint32_t max_polls;                  /* polls per wait before giving up; 0 = 4194304 (seconds) */
+  uint32_t reserved;
 } cc1d_peer_reduce;
 
 CC1D_API int64_t cc1d_peer_blocks(int64_t dim, int32_t width);

@@ -14,8 +14,9 @@ replayed from a CUDA graph:
   the unsharded causal_conv1d_fn within the dtype tolerance,
 * no bounded wait gave up.
 
-Needs two or more GPUs (one rank per GPU; two ranks on one GPU are refused
-by PeerReducer); skipped otherwise."""
+The multi-rank tests need two or more GPUs (one rank per GPU; two ranks on
+one GPU are refused by PeerReducer) and are skipped otherwise; the bounded
+wait of the exchange is tested on one GPU."""
 
 from __future__ import annotations
 
@@ -229,3 +230,49 @@ def test_one_process_several_devices():
     for other in results[1:]:
         for a, c in zip(results[0], other):
             assert torch.equal(a, c)
+
+
+def test_peer_wait_gives_up_and_reports():
+    """Failure detection of the fused reduction on one GPU, with no fault: a
+    'peer' buffer that nobody pushes into, so every bounded wait runs out
+    after max_polls.  The outputs stay unwritten, the call counters still
+    advance, the host reads the count from cc1d_device_status, and the
+    context stays usable (a following single-rank call matches the local
+    backward bitwise)."""
+    from causal_conv1d_b200 import _lib, _ops
+
+    dev = torch.device("cuda", 0)
+    B, D, L, W = 2, 256, 64, 4
+    x, w, b, init, douts = _case_inputs(torch.bfloat16, B, D, L, W, 11, True, True)
+    x, w, b, init, dout = x.to(dev), w.to(dev), b.to(dev), init.to(dev), douts[0].to(dev)
+    lib = _lib.load()
+    nblocks = int(lib.cc1d_peer_blocks(D, W))
+    _lib.device_wait_timeouts()  # reset the counter
+    own = torch.zeros(int(lib.cc1d_peer_exchange_bytes(D, W, 2)) // 8, dtype=torch.int64, device=dev)
+    silent = torch.zeros_like(own)
+    ptrs = torch.tensor([own.data_ptr(), silent.data_ptr()], dtype=torch.int64, device=dev)
+    epochs = torch.zeros(nblocks, dtype=torch.int32, device=dev)
+    dx = torch.empty_like(x)
+    dinit = torch.empty_like(init)
+    dwdb = torch.full((D * (W + 1),), float("nan"), device=dev)
+    dw = torch.full((D, W), float("nan"), dtype=torch.bfloat16, device=dev)
+    db = torch.full((D,), float("nan"), dtype=torch.bfloat16, device=dev)
+    _ops.bwd_peer(x, w, b, dout, init, None, dx, dwdb, dinit, dw, db, True, ptrs, epochs, 0, 2, 1024)
+    torch.cuda.synchronize(dev)
+    assert _lib.device_wait_timeouts() > 0
+    assert torch.isnan(dwdb).all() and torch.isnan(dw).all() and torch.isnan(db).all()
+    assert torch.equal(epochs.cpu(), torch.ones(nblocks, dtype=torch.int32))
+    # dx does not depend on the exchange: it is complete.
+    ref_dx, ref_dwdb = torch.empty_like(x), torch.empty(D * (W + 1), device=dev)
+    ref_dinit = torch.empty_like(init)
+    _ops.bwd(x, w, b, dout, None, init, None, ref_dx, ref_dwdb, ref_dinit, None, None, True)
+    assert torch.equal(dx, ref_dx) and torch.equal(dinit, ref_dinit)
+    # The context is intact: a world of one reduces to the local result.
+    one = torch.zeros_like(own)
+    _ops.bwd_peer(x, w, b, dout, init, None, dx, dwdb, dinit, dw, db, True,
+                  torch.tensor([one.data_ptr()], dtype=torch.int64, device=dev),
+                  torch.zeros(nblocks, dtype=torch.int32, device=dev), 0, 1)
+    torch.cuda.synchronize(dev)
+    assert _lib.device_wait_timeouts() == 0
+    assert torch.equal(dwdb, ref_dwdb)
+    assert torch.equal(dw, ref_dwdb[: D * W].view(D, W).to(torch.bfloat16))
