@@ -228,6 +228,24 @@ __global__ void __launch_bounds__(kThreadsTma, CC1D_FWD_MIN_BLOCKS) fwd_chan_tma
           xw[H - 1] = xv;
           sw[H - 1] = sid;
         }
+      } else if (nr == TR && valid) {
+        // Full tile, in-range channels: no per-row checks; row addresses are
+        // the tile's base plus compile-time multiples of the row pitch.
+        const i64 pitch = a.os_l;
+#pragma unroll
+        for (int rr = 0; rr < TR; ++rr) {
+          const float2 xv = P::unpack(tile[rr * ROW_WORDS]);
+          float2 acc = bv;
+#pragma unroll
+          for (int j = 0; j < H; ++j) acc = fma2(wv[j], xw[j], acc);
+          acc = fma2(wv[H], xv, acc);
+          if (SILU) acc = silu2(acc);
+          *reinterpret_cast<PW*>(orow + rr * pitch) = P::pack(acc);
+#pragma unroll
+          for (int j = 0; j < H - 1; ++j) xw[j] = xw[j + 1];
+          xw[H - 1] = xv;
+        }
+        orow += TR * pitch;
       } else {
 #pragma unroll
         for (int rr = 0; rr < TR; ++rr) {
