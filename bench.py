@@ -392,6 +392,30 @@ def time_kernels(peak):
     del states, xs, outs
     torch.cuda.empty_cache()
 
+    # Next rows of the path: a 4-token decode burst (speculative decoding) on
+    # the C3a pool, and the C3a step with a channel-last conv_state pool
+    # (strides (3*D, 1, D)); both use the generic update kernel.
+    Lb = 4
+    xs = [rn(Bu, Du, Lb) for _ in range(sets)]
+    pools = [rn(512, Du, W - 1) for _ in range(sets)]
+    outs = [torch.empty_like(xs[0]) for _ in range(sets)]
+    ms = _kernel_ms(lambda i: _ops.update(xs[i], pools[i], w, b, None, idx[i], outs[i], True), 800, sets)
+    nbytes = Bu * Du * (2 * Lb + 2 * Lb + 6 + 6) + Du * (W + 1) * 2 + Bu * 4
+    res["update_burst4_indexed"] = dict(ms=ms, gbs=nbytes / ms / 1e6, frac=nbytes / ms / 1e6 / peak,
+                                        tokens_per_s=Bu * Lb / (ms / 1e3), algorithmic_bytes=nbytes,
+                                        note="x (256, 5376, 4), pool (512, 5376, 3), generic update kernel")
+    del xs, pools, outs
+    xs = [rn(Bu, Du, 1) for _ in range(sets)]
+    pools = [rn(512, W - 1, Du).transpose(1, 2) for _ in range(sets)]
+    outs = [torch.empty_like(xs[0]) for _ in range(sets)]
+    ms = _kernel_ms(lambda i: _ops.update(xs[i], pools[i], w, b, None, idx[i], outs[i], True), 800, sets)
+    nbytes = Bu * Du * (2 + 2 + 6 + 6) + Du * (W + 1) * 2 + Bu * 4
+    res["update_c3a_chanlast_state"] = dict(ms=ms, gbs=nbytes / ms / 1e6, frac=nbytes / ms / 1e6 / peak,
+                                            tokens_per_s=Bu / (ms / 1e3), algorithmic_bytes=nbytes,
+                                            note="C3a with conv_state pool stored (512, 3, 5376), generic kernel")
+    del xs, pools, outs
+    torch.cuda.empty_cache()
+
     # C4: varlen packed prefill fp16 (1, 4096, 65536) channel-last + seq_idx.
     dt = torch.float16
     Lv, Dv = 65536, 4096
@@ -415,6 +439,15 @@ def time_kernels(peak):
     nb = 6 * n + Lv * 4 + Dv * (W + 1) * 2 * 2 + Dv * (W + 1) * 4
     res["bwd_c4_varlen"] = dict(ms=ms, gbs=nb / ms / 1e6, frac=nb / ms / 1e6 / peak, tokens_per_s=Lv / (ms / 1e3),
                                 algorithmic_bytes=nb)
+    # varlen states hand-off of the C4 batch: the last W-1 tokens of each of
+    # the 32 packed sequences -> (32, 4096, 3) conv states.
+    tok = x.transpose(1, 2)[0]  # (65536, 4096) token-major view
+    cu = torch.cat([torch.zeros(1, dtype=torch.int32), lens.cumsum(0).to(torch.int32)]).cuda()
+    st = torch.empty(32, W - 1, Dv, dtype=dt, device="cuda").transpose(1, 2)
+    ms = _kernel_ms(lambda i: _ops.varlen_states(tok, cu, st), 200, 1)
+    nb = 2 * 32 * Dv * (W - 1) * 2 + 33 * 4
+    res["varlen_states_c4"] = dict(ms=ms, gbs=nb / ms / 1e6, frac=nb / ms / 1e6 / peak, algorithmic_bytes=nb,
+                                   note="32 sequences, state_len 3, dim 4096 fp16; launch-latency bound")
     del x, dout, out, dx
     torch.cuda.empty_cache()
 

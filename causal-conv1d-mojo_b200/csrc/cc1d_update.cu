@@ -101,6 +101,104 @@ __global__ void __launch_bounds__(128) update_kernel(const UpdateArgs a) {
   }
 }
 
+// Linear-mode decode step for short bursts (seqlen <= kLinLMax) and short
+// states (state_len <= kLinSMax), any strides: one thread per (b, c); every
+// load (the W-1 history, the whole old state row, the burst's x, weights,
+// bias) is issued before any store, so a thread has one memory round trip
+// after the pool index, and a warp's accesses cover 32 consecutive channels
+// whatever the layout (packed rows, or channel-last state with unit channel
+// stride).  Same tap order and SiLU as update_kernel.
+constexpr int kLinLMax = 8;
+constexpr int kLinSMax = 16;
+
+// A 16-bit or 32-bit element, given its bits in the low bits of `h`.
+template <typename T>
+__device__ __forceinline__ float bits_to_float(uint32_t h);
+template <>
+__device__ __forceinline__ float bits_to_float<float>(uint32_t h) { return __uint_as_float(h); }
+template <>
+__device__ __forceinline__ float bits_to_float<__nv_bfloat16>(uint32_t h) { return __uint_as_float(h << 16); }
+template <>
+__device__ __forceinline__ float bits_to_float<__half>(uint32_t h) {
+  return __half2float(__ushort_as_half((unsigned short)h));
+}
+
+// Raw bits of one element (state values are copied bit for bit).
+template <typename T>
+struct RawElem {
+  typedef unsigned short type;
+};
+template <>
+struct RawElem<float> {
+  typedef unsigned int type;
+};
+template <typename T>
+__device__ __forceinline__ float raw_to_float(typename RawElem<T>::type r) {
+  return bits_to_float<T>((uint32_t)r);
+}
+
+// SFIX > 0: state_len == SFIX known at compile time (the serving layout
+// state_len == W-1); 0: any state_len <= kLinSMax.  Grid (channel blocks,
+// batch).
+template <typename T, int W, int SFIX>
+__global__ void __launch_bounds__(128) update_lin_kernel(const UpdateArgs a) {
+  typedef typename RawElem<T>::type R;
+  constexpr int H = W - 1;
+  constexpr int SM = SFIX > 0 ? SFIX : kLinSMax;
+  const i64 b = blockIdx.y;
+  const i64 c = (i64)blockIdx.x * blockDim.x + threadIdx.x;
+  if (c >= a.D) return;
+  const int L = (int)a.L, S = SFIX > 0 ? SFIX : (int)a.S;
+  T* __restrict__ ob = static_cast<T*>(a.out) + b * a.os_b + c * a.os_c;
+  i64 row = b;
+  if (a.idx != nullptr) {
+    const int r = a.idx[b];
+    if (r < 0 || r >= a.state_rows) {
+#pragma unroll
+      for (int i = 0; i < kLinLMax; ++i)
+        if (i < L) ob[i * a.os_l] = Cvt<T>::to(0.f);
+      return;
+    }
+    row = r;
+  }
+  R* __restrict__ st = reinterpret_cast<R*>(static_cast<T*>(a.state) + row * a.ss_b + c * a.ss_c);
+  const R* __restrict__ xb = reinterpret_cast<const R*>(static_cast<const T*>(a.x) + b * a.xs_b + c * a.xs_c);
+  // The state is held right-aligned in a shift register: reg[SM-S .. SM-1]
+  // = old state; every register index below is a compile-time constant.
+  R reg[SM], xv[kLinLMax];
+#pragma unroll
+  for (int q = 0; q < SM; ++q) {
+    const int j = q - (SM - S);
+    reg[q] = j >= 0 ? st[j * a.ss_l] : (R)0;
+  }
+#pragma unroll
+  for (int i = 0; i < kLinLMax; ++i) xv[i] = i < L ? xb[i * a.xs_l] : (R)0;
+  float wv[W];
+#pragma unroll
+  for (int k = 0; k < W; ++k) wv[k] = Cvt<T>::f(static_cast<const T*>(a.w)[c * a.ws_c + k * a.ws_k]);
+  const float bv = a.bias ? Cvt<T>::f(static_cast<const T*>(a.bias)[c * a.bs]) : 0.f;
+#pragma unroll
+  for (int i = 0; i < kLinLMax; ++i) {
+    if (i < L) {
+      float acc = bv;
+#pragma unroll
+      for (int k = 0; k < H; ++k) acc = fmaf(wv[k], raw_to_float<T>(reg[SM - H + k]), acc);
+      acc = fmaf(wv[H], raw_to_float<T>(xv[i]), acc);
+      if (a.silu) acc = silu_f(acc);
+      ob[i * a.os_l] = Cvt<T>::to(acc);
+#pragma unroll
+      for (int q = 0; q < SM - 1; ++q) reg[q] = reg[q + 1];
+      reg[SM - 1] = xv[i];
+    }
+  }
+  // New state = the last S values of cat([old, x]) = reg[SM-S .. SM-1].
+#pragma unroll
+  for (int q = 0; q < SM; ++q) {
+    const int j = q - (SM - S);
+    if (j >= 0) st[j * a.ss_l] = reg[q];
+  }
+}
+
 // Largest vector (in elements, a power of two, at most 16 bytes) that
 // divides a run of N contiguous elements of T.
 template <typename T, int N>
@@ -291,18 +389,6 @@ __global__ void __launch_bounds__(128) update_circ_kernel(const UpdateArgs a) {
       st[c * a.ss_c + cs * a.ss_l] = xv[v];
     }
   }
-}
-
-// A 16-bit or 32-bit element, given its bits in the low bits of `h`.
-template <typename T>
-__device__ __forceinline__ float bits_to_float(uint32_t h);
-template <>
-__device__ __forceinline__ float bits_to_float<float>(uint32_t h) { return __uint_as_float(h); }
-template <>
-__device__ __forceinline__ float bits_to_float<__nv_bfloat16>(uint32_t h) { return __uint_as_float(h << 16); }
-template <>
-__device__ __forceinline__ float bits_to_float<__half>(uint32_t h) {
-  return __half2float(__ushort_as_half((unsigned short)h));
 }
 
 // Element `i` of a state row held in NW 32-bit words (selects, no local
@@ -540,6 +626,14 @@ struct LaunchUpdate {
       const i64 blocks = ceil_div(a.D, (i64)threads * 8) * a.B;
       if (blocks > 0x7fffffffLL) return cudaErrorInvalidConfiguration;
       update_circ_kernel<T, W><<<(unsigned)blocks, threads, 0, stream>>>(a);
+      return cudaGetLastError();
+    }
+    if (a.cache_seqlens == nullptr && a.L >= 1 && a.L <= kLinLMax && a.S <= kLinSMax && a.B <= 65535) {
+      const dim3 grid((unsigned)ceil_div(a.D, (i64)threads), (unsigned)a.B);
+      if (a.S == W - 1)
+        update_lin_kernel<T, W, W - 1><<<grid, threads, 0, stream>>>(a);
+      else
+        update_lin_kernel<T, W, 0><<<grid, threads, 0, stream>>>(a);
       return cudaGetLastError();
     }
     const i64 blocks = ceil_div(a.D, (i64)threads) * a.B;

@@ -200,3 +200,40 @@ def test_circular_serving_state_len_vs_oracle(dtype, W, pool, row_bytes, D):
     assert_bitwise(st_g.cpu(), st_o, "conv_state")
     if pool:
         assert torch.count_nonzero(big_g[:, 1::2]) == 0  # the interleaved rows are never written
+
+
+@pytest.mark.parametrize("pool", [False, True])
+@pytest.mark.parametrize("L,S,state_layout", [
+    (4, 3, "packed"), (4, 3, "chanlast"), (1, 3, "chanlast"), (8, 16, "packed"), (5, 12, "chanlast"),
+    (2, 9, "packed"),       # burst shorter than the state: old values shift left
+    (12, 20, "packed"),     # past the burst kernel's limits: generic kernel
+])
+@pytest.mark.parametrize("dtype", ["fp32", "bf16"])
+def test_linear_burst_and_state_layouts_vs_oracle(dtype, L, S, state_layout, pool):
+    """Linear-mode decode bursts (speculative decoding) and conv_state pools
+    stored channel-last (strides (S*D, 1, D)): outputs within tolerance,
+    state rows bit-exact, untouched and padding rows unchanged."""
+    dt = DTYPES[dtype]
+    B, D, W = 6, 328, 4
+    rows = 2 * B if pool else B
+    x = seeded((B, D, L), dt, 21)
+    w = seeded((D, W), dt, 22, "uniform")
+    b = seeded((D,), dt, 23, "uniform")
+    state = seeded((rows, D, S), dt, 24)
+    idx = None
+    if pool:
+        idx = torch.randperm(rows, generator=torch.Generator().manual_seed(5))[:B].to(torch.int32)
+        idx[1] = -1
+    if state_layout == "chanlast":
+        st_g = state.transpose(1, 2).contiguous().transpose(1, 2).to(DEV)
+        assert st_g.stride(1) == 1
+    else:
+        st_g = state.to(DEV)
+    out = causal_conv1d_update(x.to(DEV), st_g, w.to(DEV), b.to(DEV), activation="silu",
+                               conv_state_indices=idx.to(DEV) if idx is not None else None)
+    st_o = state.clone()
+    o = oracle.update(x, st_o, w, b, silu=True, cache_seqlens=None, conv_state_indices=idx)
+    assert_close(out.cpu(), o, dt, "out")
+    assert_bitwise(st_g.cpu(), st_o, "conv_state")
+    if idx is not None:
+        assert torch.all(out[1] == 0)
