@@ -502,6 +502,8 @@ constexpr int kFinWarps = 8;
 template <typename T, int W>
 __global__ void __launch_bounds__(kFinWarps * 32) finalize_kernel(const FinalizeArgs a) {
   __shared__ float part[kFinWarps][32];
+  griddep_wait();  // the partials come from the backward kernel just before
+  griddep_launch_dependents();
   const i64 n = a.D * (W + 1);
   const int lane = threadIdx.x & 31;
   const int warp = threadIdx.x >> 5;
@@ -683,8 +685,7 @@ struct LaunchFinalize {
   cudaError_t operator()() {
     const i64 n = a.D * (W + 1);
     if (n == 0) return cudaSuccess;
-    finalize_kernel<T, W><<<(unsigned)ceil_div(n, (i64)32), kFinWarps * 32, 0, stream>>>(a);
-    return cudaGetLastError();
+    return launch_pdl(finalize_kernel<T, W>, dim3((unsigned)ceil_div(n, (i64)32)), dim3(kFinWarps * 32), 0, stream, a);
   }
 };
 

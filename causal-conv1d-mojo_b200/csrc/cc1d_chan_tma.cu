@@ -122,6 +122,8 @@ __global__ void __launch_bounds__(kThreadsTma, CC1D_FWD_MIN_BLOCKS) fwd_chan_tma
     fence_mbar_init();
   }
   __syncthreads();
+  griddep_wait();  // inputs of this launch may come from the previous kernel
+  griddep_launch_dependents();
 
   if (warp == kCW) {
     // Producer: one elected lane issues every tile of this block.
@@ -383,6 +385,8 @@ __global__ void __launch_bounds__(kThreadsTma, CC1D_BWD_MIN_BLOCKS) bwd_chan_tma
     fence_mbar_init();
   }
   __syncthreads();
+  griddep_wait();  // inputs of this launch may come from the previous kernel
+  griddep_launch_dependents();
 
   if (warp == kCW) {
     if (lane == 0) {
@@ -628,8 +632,8 @@ cudaError_t fwd_instance(FwdTmaParams* prm, const Plan* plan, cudaStream_t strea
   if (e != cudaSuccess) return e;
   if (nb_out) *nb_out = nb;
   if (prm == nullptr) return cudaSuccess;
-  fwd_chan_tma_kernel<T, W, SEQ, SILU><<<(unsigned)plan->grid, kThreadsTma, smem, stream>>>(*prm);
-  return cudaGetLastError();
+  return launch_pdl(fwd_chan_tma_kernel<T, W, SEQ, SILU>, dim3((unsigned)plan->grid), dim3(kThreadsTma), smem, stream,
+                    *prm);
 }
 
 template <typename T, int W, bool SEQ, bool SILU>
@@ -642,8 +646,8 @@ cudaError_t bwd_instance(BwdTmaParams* prm, const Plan* plan, cudaStream_t strea
   if (e != cudaSuccess) return e;
   if (nb_out) *nb_out = nb;
   if (prm == nullptr) return cudaSuccess;
-  bwd_chan_tma_kernel<T, W, SEQ, SILU><<<(unsigned)plan->grid, kThreadsTma, smem, stream>>>(*prm);
-  return cudaGetLastError();
+  return launch_pdl(bwd_chan_tma_kernel<T, W, SEQ, SILU>, dim3((unsigned)plan->grid), dim3(kThreadsTma), smem, stream,
+                    *prm);
 }
 
 struct FwdTmaOp {

@@ -21,6 +21,13 @@ constexpr unsigned kFull = 0xffffffffu;
 // of a position whose value matters (values there are zero).
 constexpr int kNoSeq = (int)0x80000000;
 
+// Programmatic dependent launch (kernels started with launch_pdl): wait
+// until the previous kernel in the stream has completed and its memory is
+// visible (a no-op for a normal launch); and let the next kernel be
+// scheduled once every block of this one has signalled or exited.
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void griddep_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 template <typename T>
 struct Cvt;
 template <>

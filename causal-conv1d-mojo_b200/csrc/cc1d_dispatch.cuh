@@ -2,6 +2,7 @@
 #pragma once
 
 #include <atomic>
+#include <utility>
 
 #include "cc1d_common.cuh"
 #include "cc1d_internal.h"
@@ -36,6 +37,26 @@ cudaError_t dispatch(int dtype, int width, F&& f) {
     case 2: return dispatch_width<float>(width, f);
     default: return cudaErrorInvalidValue;
   }
+}
+
+// Launch with programmatic stream serialization (PDL): the kernel may be
+// scheduled while the previous kernel in the stream drains, and must call
+// griddep_wait() before touching global memory.  Captured into CUDA graphs
+// as a programmatic edge.
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                       Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
 }
 
 // Resident blocks per SM for `kernel` at `threads` threads and `smem` bytes

@@ -50,6 +50,8 @@ __device__ __forceinline__ unsigned long long ld_relaxed_sys_u64(const unsigned 
 template <typename T, int W>
 __global__ void __launch_bounds__(kPeerWarps * 32) finalize_peer_kernel(const PeerFinalizeArgs p) {
   __shared__ float part[kPeerWarps][32];
+  griddep_wait();  // the partials come from the backward kernel just before
+  griddep_launch_dependents();
   const FinalizeArgs& a = p.f;
   const i64 n = a.D * (W + 1);
   const i64 nchunks = ceil_div(n, (i64)32);
@@ -127,8 +129,7 @@ struct LaunchPeer {
   cudaStream_t stream;
   template <typename T, int W>
   cudaError_t operator()() {
-    finalize_peer_kernel<T, W><<<(unsigned)p.nblocks, kPeerWarps * 32, 0, stream>>>(p);
-    return cudaGetLastError();
+    return launch_pdl(finalize_peer_kernel<T, W>, dim3((unsigned)p.nblocks), dim3(kPeerWarps * 32), 0, stream, p);
   }
 };
 

@@ -177,6 +177,8 @@ __global__ void __launch_bounds__(kThreadsSeq, CC1D_SEQ_FWD_MIN_BLOCKS) fwd_seq_
     fence_mbar_init();
   }
   __syncthreads();
+  griddep_wait();  // inputs of this launch may come from the previous kernel
+  griddep_launch_dependents();
 
   if (warp == kSW) {
     if (lane == 0) {
@@ -321,6 +323,8 @@ __global__ void __launch_bounds__(kThreadsSeq, W <= 5 ? CC1D_SEQ_BWD_MIN_BLOCKS 
     fence_mbar_init();
   }
   __syncthreads();
+  griddep_wait();  // inputs of this launch may come from the previous kernel
+  griddep_launch_dependents();
 
   if (warp == kSW) {
     if (lane == 0) {
@@ -590,8 +594,7 @@ cudaError_t seq_fwd_instance(SeqFwdParams* prm, const Plan* plan, cudaStream_t s
   if (e != cudaSuccess) return e;
   if (nb_out) *nb_out = nb;
   if (prm == nullptr) return cudaSuccess;
-  fwd_seq_tma_kernel<T, W, SILU><<<(unsigned)plan->grid, kThreadsSeq, smem, stream>>>(*prm);
-  return cudaGetLastError();
+  return launch_pdl(fwd_seq_tma_kernel<T, W, SILU>, dim3((unsigned)plan->grid), dim3(kThreadsSeq), smem, stream, *prm);
 }
 
 template <typename T, int W, bool SILU>
@@ -605,8 +608,7 @@ cudaError_t seq_bwd_instance(SeqBwdParams* prm, const Plan* plan, cudaStream_t s
   if (e != cudaSuccess) return e;
   if (nb_out) *nb_out = nb;
   if (prm == nullptr) return cudaSuccess;
-  bwd_seq_tma_kernel<T, W, SILU><<<(unsigned)plan->grid, kThreadsSeq, smem, stream>>>(*prm);
-  return cudaGetLastError();
+  return launch_pdl(bwd_seq_tma_kernel<T, W, SILU>, dim3((unsigned)plan->grid), dim3(kThreadsSeq), smem, stream, *prm);
 }
 
 struct SeqFwdOp {

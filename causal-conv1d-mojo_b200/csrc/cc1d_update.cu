@@ -142,6 +142,8 @@ __device__ __forceinline__ float raw_to_float(typename RawElem<T>::type r) {
 // batch).
 template <typename T, int W, int SFIX>
 __global__ void __launch_bounds__(128) update_lin_kernel(const UpdateArgs a) {
+  griddep_wait();  // inputs and state may come from the previous kernel
+  griddep_launch_dependents();
   typedef typename RawElem<T>::type R;
   constexpr int H = W - 1;
   constexpr int SM = SFIX > 0 ? SFIX : kLinSMax;
@@ -233,6 +235,8 @@ constexpr int kVecV = CC1D_VEC_V;
 // (only the state row waits for the pool index).
 template <typename T, int W>
 __global__ void __launch_bounds__(128, CC1D_VEC_MIN_BLOCKS) update_vec_kernel(const UpdateArgs a) {
+  griddep_wait();  // inputs and state may come from the previous kernel
+  griddep_launch_dependents();
   constexpr int H = W - 1;
   constexpr int V = kVecV;
   constexpr int EX = vec_elems<T, V>();
@@ -450,6 +454,8 @@ template <typename T, int W, int NW>
 __global__ void __launch_bounds__(128, CC1D_CIRC_MIN_BLOCKS) update_circ_row_kernel(const UpdateArgs a,
                                                                                    const i64 warps_per_row,
                                                                                    const bool taps_vec) {
+  griddep_wait();  // inputs and state may come from the previous kernel
+  griddep_launch_dependents();
   constexpr int H = W - 1;
   constexpr int V = circ_lane_channels<NW>();  // channels per lane
   const i64 gw = ((i64)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
@@ -604,8 +610,7 @@ struct LaunchUpdate {
     if (vec_path_ok<T, W>(a)) {
       const i64 blocks = ceil_div(a.D / kVecV, (i64)threads) * a.B;
       if (blocks > 0x7fffffffLL) return cudaErrorInvalidConfiguration;
-      update_vec_kernel<T, W><<<(unsigned)blocks, threads, 0, stream>>>(a);
-      return cudaGetLastError();
+      return launch_pdl(update_vec_kernel<T, W>, dim3((unsigned)blocks), dim3(threads), 0, stream, a);
     }
     const int nw = circ_row_words<T>(a);
     if (nw == 4 || nw == 8) {
@@ -617,10 +622,10 @@ struct LaunchUpdate {
       const bool taps_vec = a.ws_k == 1 && (tb == 4 || tb == 8 || tb == 16) && (a.ws_c * (i64)sizeof(T)) % tb == 0 &&
                             (reinterpret_cast<uintptr_t>(a.w) % (uintptr_t)tb) == 0;
       if (nw == 4)
-        update_circ_row_kernel<T, W, 4><<<(unsigned)blocks, threads, 0, stream>>>(a, warps_per_row, taps_vec);
-      else
-        update_circ_row_kernel<T, W, 8><<<(unsigned)blocks, threads, 0, stream>>>(a, warps_per_row, taps_vec);
-      return cudaGetLastError();
+        return launch_pdl(update_circ_row_kernel<T, W, 4>, dim3((unsigned)blocks), dim3(threads), 0, stream, a,
+                          warps_per_row, taps_vec);
+      return launch_pdl(update_circ_row_kernel<T, W, 8>, dim3((unsigned)blocks), dim3(threads), 0, stream, a,
+                        warps_per_row, taps_vec);
     }
     if (a.cache_seqlens != nullptr && a.L == 1) {
       const i64 blocks = ceil_div(a.D, (i64)threads * 8) * a.B;
@@ -630,11 +635,8 @@ struct LaunchUpdate {
     }
     if (a.cache_seqlens == nullptr && a.L >= 1 && a.L <= kLinLMax && a.S <= kLinSMax && a.B <= 65535) {
       const dim3 grid((unsigned)ceil_div(a.D, (i64)threads), (unsigned)a.B);
-      if (a.S == W - 1)
-        update_lin_kernel<T, W, W - 1><<<grid, threads, 0, stream>>>(a);
-      else
-        update_lin_kernel<T, W, 0><<<grid, threads, 0, stream>>>(a);
-      return cudaGetLastError();
+      if (a.S == W - 1) return launch_pdl(update_lin_kernel<T, W, W - 1>, grid, dim3(threads), 0, stream, a);
+      return launch_pdl(update_lin_kernel<T, W, 0>, grid, dim3(threads), 0, stream, a);
     }
     const i64 blocks = ceil_div(a.D, (i64)threads) * a.B;
     if (blocks > 0x7fffffffLL) return cudaErrorInvalidConfiguration;
