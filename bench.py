@@ -608,12 +608,16 @@ def run_only(args):
         dw, db = torch.empty(Dv, W, dtype=dt, device="cuda"), torch.empty(Dv, dtype=dt, device="cuda")
         fn = (lambda: _ops.fwd(x, wv, bv, seq, None, out, True, None)) if op == "fwd_c4" else \
             (lambda: _ops.bwd(x, wv, bv, dout, seq, None, None, dx, dwdb, None, dw, db, True))
-    elif op in ("update_c3a", "update_c3b"):
+    elif op in ("update_c3a", "update_c3b", "update_burst4", "update_c3a_chanlast"):
         Bu, Du = 256, 5376
         w, b = ru(Du, W), ru(Du)
-        x = rn(Bu, Du, 1)
+        x = rn(Bu, Du, 4 if op == "update_burst4" else 1)
         out = torch.empty_like(x)
-        if op == "update_c3a":
+        if op in ("update_burst4", "update_c3a_chanlast"):
+            pool = rn(512, Du, W - 1) if op == "update_burst4" else rn(512, W - 1, Du).transpose(1, 2)
+            idx = torch.randperm(512, device="cuda")[:Bu].to(torch.int32)
+            fn = lambda: _ops.update(x, pool, w, b, None, idx, out, True)  # noqa: E731
+        elif op == "update_c3a":
             pool = rn(512, Du, W - 1)
             idx = torch.randperm(512, device="cuda")[:Bu].to(torch.int32)
             fn = lambda: _ops.update(x, pool, w, b, None, idx, out, True)  # noqa: E731
@@ -656,8 +660,9 @@ def main():
     ap.add_argument("--skip-e2e", action="store_true")
     ap.add_argument("--skip-cpu", action="store_true")
     ap.add_argument("--only", default=None,
-                    help="launch one op alone (fwd_c2, bwd_c2, update_c3a, update_c3b, fwd_c4, bwd_c4, fwd_c5, "
-                         "bwd_c5) --reps times, for profilers; prints no contract line")
+                    help="launch one op alone (fwd_c2, bwd_c2, update_c3a, update_c3b, update_burst4, "
+                         "update_c3a_chanlast, fwd_c4, bwd_c4, fwd_c5, bwd_c5) --reps times, for profilers; "
+                         "prints no contract line")
     ap.add_argument("--reps", type=int, default=3)
     ap.add_argument("--c5-batch", type=int, default=64, help="batch of the C5 shape in --only mode")
     args = ap.parse_args()

@@ -138,9 +138,10 @@ __device__ __forceinline__ float raw_to_float(typename RawElem<T>::type r) {
 }
 
 // SFIX > 0: state_len == SFIX known at compile time (the serving layout
-// state_len == W-1); 0: any state_len <= kLinSMax.  Grid (channel blocks,
-// batch).
-template <typename T, int W, int SFIX>
+// state_len == W-1); 0: any state_len <= kLinSMax.  LFIX > 0: seqlen ==
+// LFIX (no predicated-off token iterations are issued); 0: any seqlen <=
+// kLinLMax.  Grid (channel blocks, batch).
+template <typename T, int W, int SFIX, int LFIX>
 __global__ void __launch_bounds__(128) update_lin_kernel(const UpdateArgs a) {
   griddep_wait();  // inputs and state may come from the previous kernel
   griddep_launch_dependents();
@@ -150,14 +151,15 @@ __global__ void __launch_bounds__(128) update_lin_kernel(const UpdateArgs a) {
   const i64 b = blockIdx.y;
   const i64 c = (i64)blockIdx.x * blockDim.x + threadIdx.x;
   if (c >= a.D) return;
-  const int L = (int)a.L, S = SFIX > 0 ? SFIX : (int)a.S;
+  constexpr int LM = LFIX > 0 ? LFIX : kLinLMax;
+  const int L = LFIX > 0 ? LFIX : (int)a.L, S = SFIX > 0 ? SFIX : (int)a.S;
   T* __restrict__ ob = static_cast<T*>(a.out) + b * a.os_b + c * a.os_c;
   i64 row = b;
   if (a.idx != nullptr) {
     const int r = a.idx[b];
     if (r < 0 || r >= a.state_rows) {
 #pragma unroll
-      for (int i = 0; i < kLinLMax; ++i)
+      for (int i = 0; i < LM; ++i)
         if (i < L) ob[i * a.os_l] = Cvt<T>::to(0.f);
       return;
     }
@@ -167,20 +169,20 @@ __global__ void __launch_bounds__(128) update_lin_kernel(const UpdateArgs a) {
   const R* __restrict__ xb = reinterpret_cast<const R*>(static_cast<const T*>(a.x) + b * a.xs_b + c * a.xs_c);
   // The state is held right-aligned in a shift register: reg[SM-S .. SM-1]
   // = old state; every register index below is a compile-time constant.
-  R reg[SM], xv[kLinLMax];
+  R reg[SM], xv[LM];
 #pragma unroll
   for (int q = 0; q < SM; ++q) {
     const int j = q - (SM - S);
     reg[q] = j >= 0 ? st[j * a.ss_l] : (R)0;
   }
 #pragma unroll
-  for (int i = 0; i < kLinLMax; ++i) xv[i] = i < L ? xb[i * a.xs_l] : (R)0;
+  for (int i = 0; i < LM; ++i) xv[i] = i < L ? xb[i * a.xs_l] : (R)0;
   float wv[W];
 #pragma unroll
   for (int k = 0; k < W; ++k) wv[k] = Cvt<T>::f(static_cast<const T*>(a.w)[c * a.ws_c + k * a.ws_k]);
   const float bv = a.bias ? Cvt<T>::f(static_cast<const T*>(a.bias)[c * a.bs]) : 0.f;
 #pragma unroll
-  for (int i = 0; i < kLinLMax; ++i) {
+  for (int i = 0; i < LM; ++i) {
     if (i < L) {
       float acc = bv;
 #pragma unroll
@@ -243,9 +245,8 @@ __global__ void __launch_bounds__(128, CC1D_VEC_MIN_BLOCKS) update_vec_kernel(co
   constexpr int EW = vec_elems<T, V * W>();
   constexpr int ES = vec_elems<T, V * H>();
   const i64 groups = a.D / V;
-  const i64 cblocks = ceil_div(groups, (i64)blockDim.x);
-  const i64 b = blockIdx.x / cblocks;
-  const i64 g = (blockIdx.x - b * cblocks) * blockDim.x + threadIdx.x;
+  const i64 b = blockIdx.y;  // grid (channel-group blocks, batch): no division
+  const i64 g = (i64)blockIdx.x * blockDim.x + threadIdx.x;
   if (g >= groups) return;
   const i64 c0 = g * V;
   T* __restrict__ ob = static_cast<T*>(a.out) + b * a.os_b + c0;
@@ -452,17 +453,18 @@ constexpr int circ_lane_channels() {
 
 template <typename T, int W, int NW>
 __global__ void __launch_bounds__(128, CC1D_CIRC_MIN_BLOCKS) update_circ_row_kernel(const UpdateArgs a,
-                                                                                   const i64 warps_per_row,
+                                                                                   const int warps_per_row,
                                                                                    const bool taps_vec) {
   griddep_wait();  // inputs and state may come from the previous kernel
   griddep_launch_dependents();
   constexpr int H = W - 1;
   constexpr int V = circ_lane_channels<NW>();  // channels per lane
-  const i64 gw = ((i64)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
-  const i64 b = gw / warps_per_row;
-  if (b >= a.B) return;
+  // Grid (warp groups of a batch row, batch): no division.
+  const int wr = (int)(blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5));
+  if (wr >= warps_per_row) return;
+  const i64 b = blockIdx.y;
   const int lane = threadIdx.x & 31;
-  const i64 c0 = (gw - b * warps_per_row) * (32 * V) + lane;
+  const i64 c0 = (i64)wr * (32 * V) + lane;
   const int nv = c0 >= a.D ? 0 : (int)min((i64)V, (a.D - c0 + 31) >> 5);  // channels of this lane in range
   T* __restrict__ out = static_cast<T*>(a.out) + b * a.os_b + c0 * a.os_c;
   const i64 out_step = 32 * a.os_c;
@@ -507,7 +509,7 @@ __global__ void __launch_bounds__(128, CC1D_CIRC_MIN_BLOCKS) update_circ_row_ker
       acc[v] = bp ? Cvt<T>::f(bp[v * b_step]) : 0.f;
     }
   }
-  int cs = (int)((i64)cs_raw % a.S);
+  int cs = cs_raw % (int)a.S;  // state_len is a few elements: 32-bit arithmetic
   if (cs < 0) cs += (int)a.S;
   int pos[H];
   {
@@ -607,25 +609,24 @@ struct LaunchUpdate {
   template <typename T, int W>
   cudaError_t operator()() {
     const int threads = 128;
-    if (vec_path_ok<T, W>(a)) {
-      const i64 blocks = ceil_div(a.D / kVecV, (i64)threads) * a.B;
-      if (blocks > 0x7fffffffLL) return cudaErrorInvalidConfiguration;
-      return launch_pdl(update_vec_kernel<T, W>, dim3((unsigned)blocks), dim3(threads), 0, stream, a);
+    if (a.B <= 65535 && vec_path_ok<T, W>(a)) {
+      const dim3 grid((unsigned)ceil_div(a.D / kVecV, (i64)threads), (unsigned)a.B);
+      return launch_pdl(update_vec_kernel<T, W>, grid, dim3(threads), 0, stream, a);
     }
-    const int nw = circ_row_words<T>(a);
+    const int nw = a.B <= 65535 ? circ_row_words<T>(a) : 0;
     if (nw == 4 || nw == 8) {
       const int V = nw == 4 ? circ_lane_channels<4>() : circ_lane_channels<8>();
       const i64 warps_per_row = ceil_div(a.D, (i64)32 * V);
-      const i64 blocks = ceil_div(a.B * warps_per_row, (i64)threads / 32);
-      if (blocks > 0x7fffffffLL) return cudaErrorInvalidConfiguration;
+      if (warps_per_row > 0x7fffffffLL || a.B > 65535) return cudaErrorInvalidConfiguration;
+      const dim3 blocks((unsigned)ceil_div(warps_per_row, (i64)threads / 32), (unsigned)a.B);
       const i64 tb = W * (i64)sizeof(T);
       const bool taps_vec = a.ws_k == 1 && (tb == 4 || tb == 8 || tb == 16) && (a.ws_c * (i64)sizeof(T)) % tb == 0 &&
                             (reinterpret_cast<uintptr_t>(a.w) % (uintptr_t)tb) == 0;
       if (nw == 4)
-        return launch_pdl(update_circ_row_kernel<T, W, 4>, dim3((unsigned)blocks), dim3(threads), 0, stream, a,
-                          warps_per_row, taps_vec);
-      return launch_pdl(update_circ_row_kernel<T, W, 8>, dim3((unsigned)blocks), dim3(threads), 0, stream, a,
-                        warps_per_row, taps_vec);
+        return launch_pdl(update_circ_row_kernel<T, W, 4>, blocks, dim3(threads), 0, stream, a, (int)warps_per_row,
+                          taps_vec);
+      return launch_pdl(update_circ_row_kernel<T, W, 8>, blocks, dim3(threads), 0, stream, a, (int)warps_per_row,
+                        taps_vec);
     }
     if (a.cache_seqlens != nullptr && a.L == 1) {
       const i64 blocks = ceil_div(a.D, (i64)threads * 8) * a.B;
@@ -635,8 +636,16 @@ struct LaunchUpdate {
     }
     if (a.cache_seqlens == nullptr && a.L >= 1 && a.L <= kLinLMax && a.S <= kLinSMax && a.B <= 65535) {
       const dim3 grid((unsigned)ceil_div(a.D, (i64)threads), (unsigned)a.B);
-      if (a.S == W - 1) return launch_pdl(update_lin_kernel<T, W, W - 1>, grid, dim3(threads), 0, stream, a);
-      return launch_pdl(update_lin_kernel<T, W, 0>, grid, dim3(threads), 0, stream, a);
+      if (a.S == W - 1) {
+        switch (a.L) {
+          case 1: return launch_pdl(update_lin_kernel<T, W, W - 1, 1>, grid, dim3(threads), 0, stream, a);
+          case 2: return launch_pdl(update_lin_kernel<T, W, W - 1, 2>, grid, dim3(threads), 0, stream, a);
+          case 3: return launch_pdl(update_lin_kernel<T, W, W - 1, 3>, grid, dim3(threads), 0, stream, a);
+          case 4: return launch_pdl(update_lin_kernel<T, W, W - 1, 4>, grid, dim3(threads), 0, stream, a);
+          default: break;
+        }
+      }
+      return launch_pdl(update_lin_kernel<T, W, 0, 0>, grid, dim3(threads), 0, stream, a);
     }
     const i64 blocks = ceil_div(a.D, (i64)threads) * a.B;
     if (blocks > 0x7fffffffLL) return cudaErrorInvalidConfiguration;
