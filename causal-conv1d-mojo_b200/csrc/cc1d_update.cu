@@ -235,7 +235,9 @@ constexpr int kVecV = CC1D_VEC_V;
 // rows packed, so a thread's state is one contiguous run); every run moves
 // as the widest aligned vectors that divide it.  All loads are independent
 // (only the state row waits for the pool index).
-template <typename T, int W>
+// SCL: conv_state stored channel-last (unit channel stride): a thread's
+// state is W-1 runs of V channels, one per position, ss_l apart.
+template <typename T, int W, bool SCL>
 __global__ void __launch_bounds__(128, CC1D_VEC_MIN_BLOCKS) update_vec_kernel(const UpdateArgs a) {
   griddep_wait();  // inputs and state may come from the previous kernel
   griddep_launch_dependents();
@@ -263,7 +265,7 @@ __global__ void __launch_bounds__(128, CC1D_VEC_MIN_BLOCKS) update_vec_kernel(co
     }
     row = r;
   }
-  T* __restrict__ st = static_cast<T*>(a.state) + row * a.ss_b + c0 * a.S;
+  T* __restrict__ st = static_cast<T*>(a.state) + row * a.ss_b + (SCL ? c0 : c0 * a.S);
   T xv[V], bv[V], wv[V * W], sv[V * H];
   const T* __restrict__ xp = static_cast<const T*>(a.x) + b * a.xs_b + c0;
 #pragma unroll
@@ -289,11 +291,23 @@ __global__ void __launch_bounds__(128, CC1D_VEC_MIN_BLOCKS) update_vec_kernel(co
 #pragma unroll
     for (int e = 0; e < EW; ++e) wv[i + e] = pw.v[e];
   }
+  if constexpr (SCL) {
 #pragma unroll
-  for (int i = 0; i < V * H; i += ES) {
-    const Pack<T, ES> ps = ld_pack_rw<T, ES>(st + i);
+    for (int j = 0; j < H; ++j) {
 #pragma unroll
-    for (int e = 0; e < ES; ++e) sv[i + e] = ps.v[e];
+      for (int i = 0; i < V; i += EX) {
+        const Pack<T, EX> ps = ld_pack_rw<T, EX>(st + j * a.ss_l + i);
+#pragma unroll
+        for (int e = 0; e < EX; ++e) sv[(i + e) * H + j] = ps.v[e];
+      }
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < V * H; i += ES) {
+      const Pack<T, ES> ps = ld_pack_rw<T, ES>(st + i);
+#pragma unroll
+      for (int e = 0; e < ES; ++e) sv[i + e] = ps.v[e];
+    }
   }
   // Compute (same tap order and SiLU as every other kernel).
   Pack<T, EX> po[V / EX];
@@ -316,12 +330,25 @@ __global__ void __launch_bounds__(128, CC1D_VEC_MIN_BLOCKS) update_vec_kernel(co
     for (int j = 0; j < H - 1; ++j) nv[v * H + j] = sv[v * H + j + 1];
     nv[v * H + H - 1] = xv[v];
   }
+  if constexpr (SCL) {
 #pragma unroll
-  for (int i = 0; i < V * H; i += ES) {
-    Pack<T, ES> pn;
+    for (int j = 0; j < H; ++j) {
 #pragma unroll
-    for (int e = 0; e < ES; ++e) pn.v[e] = nv[i + e];
-    st_pack<T, ES>(st + i, pn);
+      for (int i = 0; i < V; i += EX) {
+        Pack<T, EX> pn;
+#pragma unroll
+        for (int e = 0; e < EX; ++e) pn.v[e] = nv[(i + e) * H + j];
+        st_pack<T, EX>(st + j * a.ss_l + i, pn);
+      }
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < V * H; i += ES) {
+      Pack<T, ES> pn;
+#pragma unroll
+      for (int e = 0; e < ES; ++e) pn.v[e] = nv[i + e];
+      st_pack<T, ES>(st + i, pn);
+    }
   }
 }
 
@@ -576,19 +603,25 @@ bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) ==
 bool aligned_bytes(const void* p, i64 bytes) { return (reinterpret_cast<uintptr_t>(p) % (uintptr_t)bytes) == 0; }
 
 // Conditions of update_vec_kernel: one new token, linear mode with
-// state_len == W-1 and packed rows, (D, W) contiguous weights, unit channel
-// stride for x / out / bias, D a multiple of the channels per thread, and
-// every run aligned to the vector that moves it.
+// state_len == W-1, (D, W) contiguous weights, unit channel stride for
+// x / out / bias, D a multiple of the channels per thread, and every run
+// aligned to the vector that moves it.  Returns 1 for packed state rows
+// (stride 1 over state_len, rows back to back), 2 for a channel-last state
+// (unit channel stride), 0 when the kernel does not apply.
 template <typename T, int W>
-bool vec_path_ok(const UpdateArgs& a) {
+int vec_path(const UpdateArgs& a) {
   constexpr int V = kVecV;
   constexpr i64 esz = (i64)sizeof(T);
   constexpr i64 EX = vec_elems<T, V>(), EW = vec_elems<T, V * W>(), ES = vec_elems<T, V * (W - 1)>();
-  return a.cache_seqlens == nullptr && a.L == 1 && a.D % V == 0 && a.S == W - 1 && a.ss_l == 1 && a.ss_c == a.S &&
-         aligned_bytes(a.state, ES * esz) && a.ss_b % ES == 0 && a.ws_k == 1 && a.ws_c == W &&
-         aligned_bytes(a.w, EW * esz) && a.xs_c == 1 && aligned_bytes(a.x, EX * esz) &&
-         (a.B == 1 || a.xs_b % EX == 0) && a.os_c == 1 && aligned_bytes(a.out, EX * esz) &&
-         (a.B == 1 || a.os_b % EX == 0) && (a.bias == nullptr || (a.bs == 1 && aligned_bytes(a.bias, EX * esz)));
+  const bool common = a.cache_seqlens == nullptr && a.L == 1 && a.D % V == 0 && a.S == W - 1 && a.ws_k == 1 &&
+                      a.ws_c == W && aligned_bytes(a.w, EW * esz) && a.xs_c == 1 && aligned_bytes(a.x, EX * esz) &&
+                      (a.B == 1 || a.xs_b % EX == 0) && a.os_c == 1 && aligned_bytes(a.out, EX * esz) &&
+                      (a.B == 1 || a.os_b % EX == 0) &&
+                      (a.bias == nullptr || (a.bs == 1 && aligned_bytes(a.bias, EX * esz)));
+  if (!common) return 0;
+  if (a.ss_l == 1 && a.ss_c == a.S && aligned_bytes(a.state, ES * esz) && a.ss_b % ES == 0) return 1;
+  if (a.ss_c == 1 && aligned_bytes(a.state, EX * esz) && a.ss_l % EX == 0 && a.ss_b % EX == 0) return 2;
+  return 0;
 }
 
 // Circular rows of 16 or 32 bytes, unit element stride, 16-byte aligned:
@@ -609,9 +642,11 @@ struct LaunchUpdate {
   template <typename T, int W>
   cudaError_t operator()() {
     const int threads = 128;
-    if (a.B <= 65535 && vec_path_ok<T, W>(a)) {
+    const int vp = a.B <= 65535 ? vec_path<T, W>(a) : 0;
+    if (vp != 0) {
       const dim3 grid((unsigned)ceil_div(a.D / kVecV, (i64)threads), (unsigned)a.B);
-      return launch_pdl(update_vec_kernel<T, W>, grid, dim3(threads), 0, stream, a);
+      if (vp == 2) return launch_pdl(update_vec_kernel<T, W, true>, grid, dim3(threads), 0, stream, a);
+      return launch_pdl(update_vec_kernel<T, W, false>, grid, dim3(threads), 0, stream, a);
     }
     const int nw = a.B <= 65535 ? circ_row_words<T>(a) : 0;
     if (nw == 4 || nw == 8) {
