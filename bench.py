@@ -531,6 +531,20 @@ def cpu_baseline(budget_s=10.0):
                       f"({best * 1e3:.1f} ms each); oracle/cc1d_oracle.c float accumulation, OpenMP"}
 
 
+def c2_config(world):
+    """The workload both arms report (the reference arm times a bounded
+    sample of it, described in its cpu_baseline.sample)."""
+    return {
+        "workload": "C2 Mamba-2 2.7B prefill: causal_conv1d_fn fwd+bwd, bf16, x (8, 5376, 2048) channel-last, "
+                    "width 4, bias, SiLU, initial_states, return_final_states",
+        "global_batch": world * B, "seq_len": L, "dim": D, "width": W,
+        "parallelism": f"batch-sharded x{world}" + (
+            ", dweight|dbias summed over ranks inside the reduction kernel over NVLink peer memory"
+            if world > 1 else ""),
+        "l2": "inputs larger than L2 (x and grad_out are 176 MB each; L2 is 126 MB)",
+    }
+
+
 def run_reference(args):
     world, rank, _ = dist_env()
     if rank != 0:
@@ -549,12 +563,11 @@ def run_reference(args):
         "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-        "config": {"workload": "C2 Mamba-2 prefill fwd+bwd (sampled: batch row 0 of 8)", "global_batch": B,
-                   "seq_len": L, "dim": D, "width": W, "layout": "channel-last",
-                   "parallelism": "CPU, OpenMP over (b, c) rows"},
+        "config": c2_config(args.gpus),
         "cpu_baseline": {"value": value, "unit": UNIT, "cores": cores, "kind": "port",
-                         "sample": f"batch row 0 (1, {D}, {L}) of C2 per step; reference CPU algorithm "
-                                   f"(oracle/cc1d_oracle.c, restating fwd_cpu/bwd_full_cpu kernel.mojo)"},
+                         "sample": f"batch row 0 (1, {D}, {L}) of C2 per step (tokens/s of that row, all host "
+                                   f"threads); reference CPU algorithm (oracle/cc1d_oracle.c, restating "
+                                   f"fwd_cpu/bwd_full_cpu kernel.mojo)"},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -721,15 +734,7 @@ def main():
             "vs_baseline": None,
             "dtype": "bf16",
             "data": "synthetic",
-            "config": {
-                "workload": "C2 Mamba-2 2.7B prefill: causal_conv1d_fn fwd+bwd, bf16, x (8, 5376, 2048) "
-                            "channel-last, width 4, bias, SiLU, initial_states, return_final_states",
-                "global_batch": world * B, "seq_len": L, "dim": D, "width": W,
-                "parallelism": f"batch-sharded x{world}" + (
-                    ", dweight|dbias summed over ranks inside the reduction kernel over NVLink peer memory"
-                    if world > 1 else ""),
-                "l2": "inputs larger than L2 (x and grad_out are 176 MB each; L2 is 126 MB)",
-            },
+            "config": c2_config(world),
             "roofline": {
                 "bound": "hbm", "achieved": bwd_gbs, "peak": peak, "unit": "GB/s", "frac": bwd_gbs / peak,
                 "traffic": traffic, "kernel": "bwd (bwd_chan_kernel + finalize_kernel), C2",
