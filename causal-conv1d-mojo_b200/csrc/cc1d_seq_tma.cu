@@ -279,15 +279,19 @@ __device__ __forceinline__ void emit_dx(const float2 (&d)[8], const float2 (&rh)
       const int q = i + m;
       acc = fma2(wp[H - m], q < 8 ? d[q < 8 ? q : 0] : rh[q < 8 ? 0 : q - 8], acc);
     }
-    if (fa != nullptr) {
-      const i64 qf = pos + i + H - a.L;
-      if (qf >= 0 && pos + i < a.L) {
-        if (va) acc.x += Cvt<T>::f(fa[qf * a.fs_l]);
-        if (vb) acc.y += Cvt<T>::f(fa[a.fs_c + qf * a.fs_l]);
-      }
-    }
     ea[i] = acc.x;
     eb[i] = acc.y;
+  }
+  // dfinal_states reach only the last W-1 positions of the sequence.
+  if (fa != nullptr && pos + 8 + H > a.L) {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const i64 qf = pos + i + H - a.L;
+      if (qf >= 0 && pos + i < a.L) {
+        if (va) ea[i] += Cvt<T>::f(fa[qf * a.fs_l]);
+        if (vb) eb[i] += Cvt<T>::f(fa[a.fs_c + qf * a.fs_l]);
+      }
+    }
   }
   if (pos < t1) {
     if (va) stg8<T>(dxa + pos, ea);
