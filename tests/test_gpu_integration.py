@@ -182,3 +182,60 @@ def test_calls_from_a_fresh_host_thread(layout):
     assert not errors, errors
     for a, c in zip(main, got[0]):
         assert torch.equal(a, c)
+
+
+def test_dependent_chains_in_one_graph_match_synchronised_eager():
+    """Kernels are launched with programmatic dependent launch, so each one
+    may be scheduled while its predecessor drains; every kernel must still
+    see all of its predecessor's writes.  Chains whose every step consumes
+    the previous step's output -- conv over conv output, backward of that,
+    and 16 decode steps on one state (circular and linear) -- captured in
+    one CUDA graph must equal the same chain run eagerly with a
+    synchronisation after every call."""
+    from causal_conv1d_b200 import _ops
+
+    g = torch.Generator(device="cpu").manual_seed(9)
+    B, D, L, W = 2, 512, 512, 4
+
+    def mk(*s):
+        return torch.randn(*s, generator=g).to(torch.bfloat16).to(DEV)
+
+    x = mk(B, L, D).transpose(1, 2)
+    w1, w2, b = mk(D, W), mk(D, W), mk(D)
+    dout = mk(B, L, D).transpose(1, 2)
+    xs = [mk(B, D, 1) for _ in range(16)]
+    circ0, lin0 = mk(B, D, 8), mk(B, D, W - 1)
+    cache = torch.arange(B, dtype=torch.int32, device=DEV)
+
+    def chain(sync):
+        y1 = torch.empty_like(x)
+        y2 = torch.empty_like(x)
+        dx = torch.empty_like(x)
+        dwdb = torch.empty(D * (W + 1), dtype=torch.float32, device=DEV)
+        circ, lin = circ0.clone(), lin0.clone()
+        outs = [torch.empty(B, D, 1, dtype=torch.bfloat16, device=DEV) for _ in range(32)]
+
+        def step(fn):
+            fn()
+            if sync:
+                torch.cuda.synchronize()
+
+        step(lambda: _ops.fwd(x, w1, b, None, None, y1, True, None))
+        step(lambda: _ops.fwd(y1, w2, b, None, None, y2, True, None))
+        step(lambda: _ops.bwd(y1, w2, b, y2, None, None, None, dx, dwdb, None, None, None, True))
+        for i in range(16):
+            step(lambda i=i: _ops.update(xs[i], circ, w1, b, cache + i, None, outs[2 * i], True))
+            step(lambda i=i: _ops.update(xs[i], lin, w1, b, None, None, outs[2 * i + 1], True))
+        return [y1, y2, dx, dwdb, circ, lin] + outs
+
+    want = [t.clone() for t in chain(True)]
+    chain(False)  # warm-up of the capture's allocations
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        got = chain(False)
+    for _ in range(2):
+        graph.replay()
+        torch.cuda.synchronize()
+        for a_, e_ in zip(got, want):
+            assert torch.equal(a_, e_)
