@@ -14,6 +14,18 @@
 //     order as the forward kernel, so decoding token by token reproduces the
 //     forward pass bit for bit.
 //
+// The same semantics run in specialised kernels, chosen by the launcher
+// from the layout (every one issues all its loads before any store):
+//   update_vec_kernel      one token, linear, state_len W-1, packed or
+//                          channel-last pools: 4 channels per thread, vectors
+//   update_lin_kernel      linear, seqlen <= 8, state_len <= 16, any strides
+//   update_circ_row_kernel one token, circular, 16- or 32-byte state rows
+//   update_circ_kernel     one token, circular, any row size / strides
+//   update_kernel          everything else
+// Every kernel but update_circ_kernel / update_kernel is launched with
+// programmatic dependent launch (waits on griddepcontrol before touching
+// memory).
+//
 // varlen_states_kernel: one thread per (sequence, slot, channel), channel
 // fastest, so reads of x rows and writes of the (batch, state_len, dim)
 // output storage are both coalesced
