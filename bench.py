@@ -439,6 +439,24 @@ def time_kernels(peak):
     nb = 6 * n + Lv * 4 + Dv * (W + 1) * 2 * 2 + Dv * (W + 1) * 4
     res["bwd_c4_varlen"] = dict(ms=ms, gbs=nb / ms / 1e6, frac=nb / ms / 1e6 / peak, tokens_per_s=Lv / (ms / 1e3),
                                 algorithmic_bytes=nb)
+    # The same packed batch in the contiguous (B, D, L) layout (seqlen TMA
+    # kernels with the sequence-id tiles).
+    del x, dout, out, dx
+    torch.cuda.empty_cache()
+    xc, doutc = rn(1, Dv, Lv, dt=dt), rn(1, Dv, Lv, dt=dt)
+    outc, dxc = torch.empty_like(xc), torch.empty_like(xc)
+    ms = _kernel_ms(lambda i: _ops.fwd(xc, wv, bv, seq, None, outc, True, None), 10, 1)
+    nb = 4 * n + Lv * 4 + Dv * (W + 1) * 2
+    res["fwd_c4_contiguous"] = dict(ms=ms, gbs=nb / ms / 1e6, frac=nb / ms / 1e6 / peak,
+                                    tokens_per_s=Lv / (ms / 1e3), algorithmic_bytes=nb)
+    ms = _kernel_ms(lambda i: _ops.bwd(xc, wv, bv, doutc, seq, None, None, dxc, dwdb, None, dw, db, True), 10, 1)
+    nb = 6 * n + Lv * 4 + Dv * (W + 1) * 2 * 2 + Dv * (W + 1) * 4
+    res["bwd_c4_contiguous"] = dict(ms=ms, gbs=nb / ms / 1e6, frac=nb / ms / 1e6 / peak,
+                                    tokens_per_s=Lv / (ms / 1e3), algorithmic_bytes=nb)
+    x = xc.transpose(1, 2).contiguous().transpose(1, 2)  # channel-last copy for the hand-off below
+    del xc, doutc, outc, dxc
+    dout = out = dx = None
+
     # varlen states hand-off of the C4 batch: the last W-1 tokens of each of
     # the 32 packed sequences -> (32, 4096, 3) conv states.
     tok = x.transpose(1, 2)[0]  # (65536, 4096) token-major view

@@ -53,6 +53,9 @@ namespace {
 #ifndef CC1D_SEQ_BWD_MIN_BLOCKS
 #define CC1D_SEQ_BWD_MIN_BLOCKS 4  // widths <= 5: registers capped at 96, 4 blocks per SM (3 without: -16% at C5)
 #endif
+#ifndef CC1D_SEQ_BWD_IDS_MIN_BLOCKS
+#define CC1D_SEQ_BWD_IDS_MIN_BLOCKS 3  // with seq_idx (174 registers uncapped: 2 blocks per SM)
+#endif
 
 constexpr int kSW = CC1D_SEQ_WARPS;  // consumer warps
 constexpr int kRows = 2 * kSW;       // channel rows per tile
@@ -72,17 +75,62 @@ constexpr int seq_bwd_stages() {
   return sizeof(T) == 2 ? CC1D_SEQ_BWD_STAGES16 : CC1D_SEQ_BWD_STAGES32;
 }
 
+// Bytes of a stage's sequence-id tile (kTL int32 ids), present with seq_idx.
+constexpr unsigned kIdsBytes = kTL * sizeof(int);
+
 struct alignas(64) SeqFwdParams {
   CUtensorMap map_x;
+  CUtensorMap map_s;  // seq_idx as (L, 1, B) int32, when given
   FwdArgs a;
   i64 groups;
 };
 struct alignas(64) SeqBwdParams {
   CUtensorMap map_x;
   CUtensorMap map_g;
+  CUtensorMap map_s;
   BwdArgs a;
   i64 groups;
 };
+
+// The 8 sequence ids [8*lane, 8*lane+8) of a stage's id tile.
+__device__ __forceinline__ void lds_ids(const unsigned char* ids, int lane, int (&v)[8]) {
+  const int4* p = reinterpret_cast<const int4*>(ids) + 2 * lane;
+  const int4 a = p[0], b = p[1];
+  v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
+  v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+}
+
+// Halo ids of a lane (positions 8*lane-H .. 8*lane-1): from lane-1, or for
+// lane 0 from the previous tile (carry, updated to this tile's last ids).
+template <int H>
+__device__ __forceinline__ void ids_halo(const int (&sid)[8], int (&carry)[H], int (&hs)[H], int lane) {
+#pragma unroll
+  for (int j = 0; j < H; ++j) {
+    const int up = __shfl_up_sync(kFull, sid[8 - H + j], 1);
+    const int nc = __shfl_sync(kFull, sid[8 - H + j], 31);
+    hs[j] = lane == 0 ? carry[j] : up;
+    carry[j] = nc;
+  }
+}
+
+// True when the whole warp's 8 positions and their halos carry one
+// non-negative id: no sequence boundary, no padding -- the ungated math
+// applies.
+template <int H>
+__device__ __forceinline__ bool ids_uniform(const int (&sid)[8], const int (&hs)[H]) {
+  const int s0 = sid[0];
+  bool u = s0 >= 0;
+#pragma unroll
+  for (int i = 1; i < 8; ++i) u = u && sid[i] == s0;
+#pragma unroll
+  for (int j = 0; j < H; ++j) u = u && hs[j] == s0;
+  return __all_sync(kFull, u);
+}
+
+// seq_idx at position q (kNoSeq outside 0 .. L-1).
+__device__ __forceinline__ int seq_at(const int* seq, i64 ss_l, i64 q, i64 L) {
+  return (q >= 0 && q < L) ? seq[q * ss_l] : kNoSeq;
+}
 
 // The 8 positions [8*lane, 8*lane+8) of tile row r, converted to float.
 template <typename T>
@@ -150,13 +198,14 @@ __device__ __forceinline__ float2 xc_pair(const T* x, i64 xs_c, i64 xs_l, const 
 // Forward
 // ---------------------------------------------------------------------------
 
-template <typename T, int W, bool SILU>
+template <typename T, int W, bool HAS_SEQ, bool SILU>
 __global__ void __launch_bounds__(kThreadsSeq, CC1D_SEQ_FWD_MIN_BLOCKS) fwd_seq_tma_kernel(const __grid_constant__ SeqFwdParams p) {
   constexpr int H = W - 1;
   constexpr unsigned TB = seq_tile_bytes<T>();
+  constexpr unsigned SB = TB + (HAS_SEQ ? kIdsBytes : 0u);
   constexpr int NS = seq_fwd_stages<T>();
   extern __shared__ __align__(128) unsigned char smem[];
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + NS * TB);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + NS * SB);
   uint64_t* empty = full + NS;
   const FwdArgs& a = p.a;
   const int warp = threadIdx.x >> 5;
@@ -183,12 +232,14 @@ __global__ void __launch_bounds__(kThreadsSeq, CC1D_SEQ_FWD_MIN_BLOCKS) fwd_seq_
   if (warp == kSW) {
     if (lane == 0) {
       prefetch_tensormap(&p.map_x);
+      if (HAS_SEQ) prefetch_tensormap(&p.map_s);
       unsigned k = 0;
       for (i64 t = t0; t < t1; t += kTL, ++k) {
         const unsigned s = k % NS, use = k / NS;
         if (use > 0 && !mbar_wait(&empty[s], (use - 1) & 1)) return;
-        mbar_arrive_expect_tx(&full[s], TB);
-        tma_load_3d(smem + s * TB, &p.map_x, &full[s], (int)t, (int)c0, (int)b);
+        mbar_arrive_expect_tx(&full[s], SB);
+        tma_load_3d(smem + s * SB, &p.map_x, &full[s], (int)t, (int)c0, (int)b);
+        if (HAS_SEQ) tma_load_3d(smem + s * SB + TB, &p.map_s, &full[s], (int)t, 0, (int)b);
       }
     }
     return;
@@ -207,18 +258,24 @@ __global__ void __launch_bounds__(kThreadsSeq, CC1D_SEQ_FWD_MIN_BLOCKS) fwd_seq_
   const T* __restrict__ ir = a.init ? static_cast<const T*>(a.init) + b * a.is_b + ra * a.is_c : nullptr;
   T* __restrict__ oa = static_cast<T*>(a.out) + b * a.os_b + ra * a.os_c;
 
-  // Halo of lane 0 in the first tile: xc at t0-H .. t0-1.
+  // Halo of lane 0 in the first tile: xc at t0-H .. t0-1 (and its ids).
   float2 carry[H];
 #pragma unroll
   for (int j = 0; j < H; ++j) carry[j] = xc_pair(xr, a.xs_c, a.xs_l, ir, a.is_c, a.is_l, H, t0 - H + j, va, vb);
+  const int* __restrict__ seq = HAS_SEQ ? a.seq + b * a.ss_b : nullptr;
+  int scarry[H];
+#pragma unroll
+  for (int j = 0; j < H; ++j) scarry[j] = HAS_SEQ ? seq_at(seq, a.ss_l, t0 - H + j, a.L) : 0;
 
   unsigned k = 0;
   for (i64 t = t0; t < t1; t += kTL, ++k) {
     const unsigned s = k % NS, use = k / NS;
     if (!mbar_wait(&full[s], use & 1)) return;
     float xa[8], xb[8];
-    lds8<T>(smem + s * TB, 2 * warp, lane, xa);
-    lds8<T>(smem + s * TB, 2 * warp + 1, lane, xb);
+    lds8<T>(smem + s * SB, 2 * warp, lane, xa);
+    lds8<T>(smem + s * SB, 2 * warp + 1, lane, xb);
+    int sid[8];
+    if (HAS_SEQ) lds_ids(smem + s * SB + TB, lane, sid);
     __syncwarp();
     if (lane == 0) mbar_arrive(&empty[s]);
     float2 xp[8];
@@ -232,18 +289,44 @@ __global__ void __launch_bounds__(kThreadsSeq, CC1D_SEQ_FWD_MIN_BLOCKS) fwd_seq_
       h[j] = lane == 0 ? carry[j] : up;
       carry[j] = nc;
     }
+    int hs[H];
+    bool gated = false;
+    if (HAS_SEQ) {
+      ids_halo<H>(sid, scarry, hs, lane);
+      gated = !ids_uniform<H>(sid, hs);
+    }
     float oa8[8], ob8[8];
+    if (!gated) {
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      float2 acc = bp;
+      for (int i = 0; i < 8; ++i) {
+        float2 acc = bp;
 #pragma unroll
-      for (int kk = 0; kk < W; ++kk) {
-        const int q = i - H + kk;
-        acc = fma2(wp[kk], q >= 0 ? xp[q >= 0 ? q : 0] : h[q >= 0 ? 0 : q + H], acc);
+        for (int kk = 0; kk < W; ++kk) {
+          const int q = i - H + kk;
+          acc = fma2(wp[kk], q >= 0 ? xp[q >= 0 ? q : 0] : h[q >= 0 ? 0 : q + H], acc);
+        }
+        if (SILU) acc = silu2(acc);
+        oa8[i] = acc.x;
+        ob8[i] = acc.y;
       }
-      if (SILU) acc = silu2(acc);
-      oa8[i] = acc.x;
-      ob8[i] = acc.y;
+    } else {
+      // A tap counts only when its position carries the output's sequence
+      // id; padding positions (id < 0) output 0.
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const int si = sid[i];
+        float2 acc = bp;
+#pragma unroll
+        for (int kk = 0; kk < W; ++kk) {
+          const int q = i - H + kk;
+          const int sq = q >= 0 ? sid[q >= 0 ? q : 0] : hs[q >= 0 ? 0 : q + H];
+          if (sq == si) acc = fma2(wp[kk], q >= 0 ? xp[q >= 0 ? q : 0] : h[q >= 0 ? 0 : q + H], acc);
+        }
+        if (SILU) acc = silu2(acc);
+        if (si < 0) acc = f2(0.f, 0.f);
+        oa8[i] = acc.x;
+        ob8[i] = acc.y;
+      }
     }
     const i64 pos = t + 8 * lane;
     if (pos < t1) {
@@ -299,11 +382,37 @@ __device__ __forceinline__ void emit_dx(const float2 (&d)[8], const float2 (&rh)
   }
 }
 
-template <typename T, int W, bool SILU>
-__global__ void __launch_bounds__(kThreadsSeq, W <= 5 ? CC1D_SEQ_BWD_MIN_BLOCKS : 1) bwd_seq_tma_kernel(const __grid_constant__ SeqBwdParams p) {
+// emit_dx with seq_idx: dx at position q sums the taps of the outputs q+m
+// that carry q's sequence id (dpre is already 0 at padding).
+template <typename T, int W>
+__device__ __forceinline__ void emit_dx_seq(const float2 (&d)[8], const float2 (&rh)[W - 1], const int (&sd)[8],
+                                            const int (&srh)[W - 1], const float2 (&wp)[W], i64 pos, i64 t1, T* dxa,
+                                            i64 dxs_c, bool va, bool vb) {
+  constexpr int H = W - 1;
+  float ea[8], eb[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    float2 acc = f2(0.f, 0.f);
+#pragma unroll
+    for (int m = 0; m <= H; ++m) {
+      const int q = i + m;
+      const int sq = q < 8 ? sd[q < 8 ? q : 0] : srh[q < 8 ? 0 : q - 8];
+      if (sq == sd[i]) acc = fma2(wp[H - m], q < 8 ? d[q < 8 ? q : 0] : rh[q < 8 ? 0 : q - 8], acc);
+    }
+    ea[i] = acc.x;
+    eb[i] = acc.y;
+  }
+  if (pos < t1) {
+    if (va) stg8<T>(dxa + pos, ea);
+    if (vb) stg8<T>(dxa + dxs_c + pos, eb);
+  }
+}
+
+template <typename T, int W, bool HAS_SEQ, bool SILU>
+__global__ void __launch_bounds__(kThreadsSeq, W > 5 ? 1 : (HAS_SEQ ? CC1D_SEQ_BWD_IDS_MIN_BLOCKS : CC1D_SEQ_BWD_MIN_BLOCKS)) bwd_seq_tma_kernel(const __grid_constant__ SeqBwdParams p) {
   constexpr int H = W - 1;
   constexpr unsigned TB = seq_tile_bytes<T>();
-  constexpr unsigned SB = 2 * TB;
+  constexpr unsigned SB = 2 * TB + (HAS_SEQ ? kIdsBytes : 0u);
   constexpr int NS = seq_bwd_stages<T>();
   extern __shared__ __align__(128) unsigned char smem[];
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + NS * SB);
@@ -334,6 +443,7 @@ __global__ void __launch_bounds__(kThreadsSeq, W <= 5 ? CC1D_SEQ_BWD_MIN_BLOCKS 
     if (lane == 0) {
       prefetch_tensormap(&p.map_x);
       prefetch_tensormap(&p.map_g);
+      if (HAS_SEQ) prefetch_tensormap(&p.map_s);
       unsigned k = 0;
       for (i64 t = t0; t < t1; t += kTL, ++k) {
         const unsigned s = k % NS, use = k / NS;
@@ -341,6 +451,7 @@ __global__ void __launch_bounds__(kThreadsSeq, W <= 5 ? CC1D_SEQ_BWD_MIN_BLOCKS 
         mbar_arrive_expect_tx(&full[s], SB);
         tma_load_3d(smem + s * SB, &p.map_x, &full[s], (int)t, (int)c0, (int)b);
         tma_load_3d(smem + s * SB + TB, &p.map_g, &full[s], (int)t, (int)c0, (int)b);
+        if (HAS_SEQ) tma_load_3d(smem + s * SB + 2 * TB, &p.map_s, &full[s], (int)t, 0, (int)b);
       }
     }
     return;
@@ -364,17 +475,26 @@ __global__ void __launch_bounds__(kThreadsSeq, W <= 5 ? CC1D_SEQ_BWD_MIN_BLOCKS 
   float2 carry[H];
 #pragma unroll
   for (int j = 0; j < H; ++j) carry[j] = xc_pair(xr, a.xs_c, a.xs_l, ir, a.is_c, a.is_l, H, t0 - H + j, va, vb);
-  // dpre just past the segment (0 past the sequence), for lane 31's last dx.
+  const int* __restrict__ seq = HAS_SEQ ? a.seq + b * a.ss_b : nullptr;
+  int scarry[H];
+#pragma unroll
+  for (int j = 0; j < H; ++j) scarry[j] = HAS_SEQ ? seq_at(seq, a.ss_l, t0 - H + j, a.L) : 0;
+  // dpre just past the segment (0 past the sequence), for lane 31's last dx,
+  // and (with seq_idx) the ids of those positions.
   float2 rend[H];
+  int srend[H];
 #pragma unroll
   for (int j = 0; j < H; ++j) {
     const i64 q = t1 + j;
     rend[j] = f2(0.f, 0.f);
-    if (q < a.L) {
+    srend[j] = HAS_SEQ ? seq_at(seq, a.ss_l, q, a.L) : 0;
+    if (q < a.L && (!HAS_SEQ || srend[j] >= 0)) {
       float2 pre = bp;
 #pragma unroll
-      for (int kk = 0; kk < W; ++kk)
+      for (int kk = 0; kk < W; ++kk) {
+        if (HAS_SEQ && seq_at(seq, a.ss_l, q - H + kk, a.L) != srend[j]) continue;
         pre = fma2(wp[kk], xc_pair(xr, a.xs_c, a.xs_l, ir, a.is_c, a.is_l, H, q - H + kk, va, vb), pre);
+      }
       const float2 g = f2(va ? Cvt<T>::f(gr[q * a.gs_l]) : 0.f, vb ? Cvt<T>::f(gr[a.gs_c + q * a.gs_l]) : 0.f);
       rend[j] = SILU ? mul2(g, silu_grad2(pre)) : g;
     }
@@ -385,6 +505,7 @@ __global__ void __launch_bounds__(kThreadsSeq, W <= 5 ? CC1D_SEQ_BWD_MIN_BLOCKS 
   for (int k = 0; k < W; ++k) dw[k] = f2(0.f, 0.f);
   float2 db = f2(0.f, 0.f);
   float2 dprev[8];
+  int sprev[8];
   i64 tprev = -1;
 
   unsigned k = 0;
@@ -396,6 +517,8 @@ __global__ void __launch_bounds__(kThreadsSeq, W <= 5 ? CC1D_SEQ_BWD_MIN_BLOCKS 
     lds8<T>(smem + s * SB, 2 * warp + 1, lane, xb);
     lds8<T>(smem + s * SB + TB, 2 * warp, lane, ga);
     lds8<T>(smem + s * SB + TB, 2 * warp + 1, lane, gb);
+    int sid[8];
+    if (HAS_SEQ) lds_ids(smem + s * SB + 2 * TB, lane, sid);
     __syncwarp();
     if (lane == 0) mbar_arrive(&empty[s]);
     float2 xp[8], d[8];
@@ -409,21 +532,52 @@ __global__ void __launch_bounds__(kThreadsSeq, W <= 5 ? CC1D_SEQ_BWD_MIN_BLOCKS 
       h[j] = lane == 0 ? carry[j] : up;
       carry[j] = nc;
     }
+    int hs[H];
+    bool gated = false;
+    if (HAS_SEQ) {
+      ids_halo<H>(sid, scarry, hs, lane);
+      gated = !ids_uniform<H>(sid, hs);
+    }
+    if (!gated) {
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      float2 pre = bp;
+      for (int i = 0; i < 8; ++i) {
+        float2 pre = bp;
 #pragma unroll
-      for (int kk = 0; kk < W; ++kk) {
-        const int q = i - H + kk;
-        pre = fma2(wp[kk], q >= 0 ? xp[q >= 0 ? q : 0] : h[q >= 0 ? 0 : q + H], pre);
+        for (int kk = 0; kk < W; ++kk) {
+          const int q = i - H + kk;
+          pre = fma2(wp[kk], q >= 0 ? xp[q >= 0 ? q : 0] : h[q >= 0 ? 0 : q + H], pre);
+        }
+        const float2 g = f2(ga[i], gb[i]);
+        d[i] = SILU ? mul2(g, silu_grad2(pre)) : g;
+        db = add2(db, d[i]);
+#pragma unroll
+        for (int kk = 0; kk < W; ++kk) {
+          const int q = i - H + kk;
+          dw[kk] = fma2(d[i], q >= 0 ? xp[q >= 0 ? q : 0] : h[q >= 0 ? 0 : q + H], dw[kk]);
+        }
       }
-      const float2 g = f2(ga[i], gb[i]);
-      d[i] = SILU ? mul2(g, silu_grad2(pre)) : g;
-      db = add2(db, d[i]);
+    } else {
+      // Taps gated by sequence id; dpre is 0 at padding (id < 0).
 #pragma unroll
-      for (int kk = 0; kk < W; ++kk) {
-        const int q = i - H + kk;
-        dw[kk] = fma2(d[i], q >= 0 ? xp[q >= 0 ? q : 0] : h[q >= 0 ? 0 : q + H], dw[kk]);
+      for (int i = 0; i < 8; ++i) {
+        const int si = sid[i];
+        float2 pre = bp;
+#pragma unroll
+        for (int kk = 0; kk < W; ++kk) {
+          const int q = i - H + kk;
+          const int sq = q >= 0 ? sid[q >= 0 ? q : 0] : hs[q >= 0 ? 0 : q + H];
+          if (sq == si) pre = fma2(wp[kk], q >= 0 ? xp[q >= 0 ? q : 0] : h[q >= 0 ? 0 : q + H], pre);
+        }
+        const float2 g = f2(ga[i], gb[i]);
+        d[i] = SILU ? mul2(g, silu_grad2(pre)) : g;
+        if (si < 0) d[i] = f2(0.f, 0.f);
+        db = add2(db, d[i]);
+#pragma unroll
+        for (int kk = 0; kk < W; ++kk) {
+          const int q = i - H + kk;
+          const int sq = q >= 0 ? sid[q >= 0 ? q : 0] : hs[q >= 0 ? 0 : q + H];
+          if (sq == si) dw[kk] = fma2(d[i], q >= 0 ? xp[q >= 0 ? q : 0] : h[q >= 0 ? 0 : q + H], dw[kk]);
+        }
       }
     }
     // dx of the previous tile: lane 31 now has its right halo (this tile's
@@ -436,7 +590,21 @@ __global__ void __launch_bounds__(kThreadsSeq, W <= 5 ? CC1D_SEQ_BWD_MIN_BLOCKS 
         const float2 first = shfl2(d[j], 0);
         rh[j] = lane == 31 ? first : nxt;
       }
-      emit_dx<T, W>(dprev, rh, wp, tprev + 8 * lane, t1, a, dxa, fa, va, vb);
+      bool egated = false;
+      int srh[H];
+      if (HAS_SEQ) {
+#pragma unroll
+        for (int j = 0; j < H; ++j) {
+          const int nxt = __shfl_down_sync(kFull, sprev[j], 1);
+          const int first = __shfl_sync(kFull, sid[j], 0);
+          srh[j] = lane == 31 ? first : nxt;
+        }
+        egated = !ids_uniform<H>(sprev, srh);
+      }
+      if (egated)
+        emit_dx_seq<T, W>(dprev, rh, sprev, srh, wp, tprev + 8 * lane, t1, dxa, a.dxs_c, va, vb);
+      else
+        emit_dx<T, W>(dprev, rh, wp, tprev + 8 * lane, t1, a, dxa, fa, va, vb);
     }
     // dinitial_states: dpre of positions 0 .. H-1 live in lane 0 of tile 0.
     if (t == 0 && lane == 0 && a.dinit != nullptr) {
@@ -455,7 +623,10 @@ __global__ void __launch_bounds__(kThreadsSeq, W <= 5 ? CC1D_SEQ_BWD_MIN_BLOCKS 
       }
     }
 #pragma unroll
-    for (int i = 0; i < 8; ++i) dprev[i] = d[i];
+    for (int i = 0; i < 8; ++i) {
+      dprev[i] = d[i];
+      if (HAS_SEQ) sprev[i] = sid[i];
+    }
     tprev = t;
   }
   if (tprev >= 0) {
@@ -465,7 +636,20 @@ __global__ void __launch_bounds__(kThreadsSeq, W <= 5 ? CC1D_SEQ_BWD_MIN_BLOCKS 
       const float2 nxt = shfl_down2(dprev[j], 1);
       rh[j] = lane == 31 ? rend[j] : nxt;
     }
-    emit_dx<T, W>(dprev, rh, wp, tprev + 8 * lane, t1, a, dxa, fa, va, vb);
+    bool egated = false;
+    int srh[H];
+    if (HAS_SEQ) {
+#pragma unroll
+      for (int j = 0; j < H; ++j) {
+        const int nxt = __shfl_down_sync(kFull, sprev[j], 1);
+        srh[j] = lane == 31 ? srend[j] : nxt;
+      }
+      egated = !ids_uniform<H>(sprev, srh);
+    }
+    if (egated)
+      emit_dx_seq<T, W>(dprev, rh, sprev, srh, wp, tprev + 8 * lane, t1, dxa, a.dxs_c, va, vb);
+    else
+      emit_dx<T, W>(dprev, rh, wp, tprev + 8 * lane, t1, a, dxa, fa, va, vb);
   }
   // Warp sums of the dweight / dbias partials; lane 0 writes this item's slot.
 #pragma unroll
@@ -544,6 +728,33 @@ bool seq_tensor_ok(const void* base, i64 s_c, i64 s_l, i64 s_b, i64 B, i64 D, in
          (B == 1 || ((s_b * esz) % 16 == 0 && s_b > 0)) && (s_c * esz) < (1LL << 40) && (s_b * esz) < (1LL << 40);
 }
 
+// 3-D map over seq_idx viewed as (L, 1, B) int32; box (256, 1, 1), zero
+// fill past the end (only positions past L read it; their outputs are not
+// stored and their dout is zero-filled too).
+bool make_ids_map(CUtensorMap* m, const int* base, i64 L, i64 B, i64 s_b) {
+  PFN_cuTensorMapEncodeTiled_v12000 enc = encode_fn();
+  if (enc == nullptr) return false;
+  if (B == 1) s_b = L;
+  cuuint64_t dims[3] = {(cuuint64_t)L, 1, (cuuint64_t)B};
+  cuuint64_t strides[2] = {(cuuint64_t)(L * 4), (cuuint64_t)(s_b * 4)};
+  cuuint32_t box[3] = {(cuuint32_t)kTL, 1, 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  const CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_INT32, 3, const_cast<int*>(base), dims, strides, box, estr,
+                         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    set_error_detail("cuTensorMapEncodeTiled returned %d for seq_idx (L %lld, B %lld)", (int)r, (long long)L,
+                     (long long)B);
+  return r == CUDA_SUCCESS;
+}
+
+// seq_idx that the id tiles can stream: unit position stride, 16-byte
+// aligned rows.
+bool ids_ok(const int* seq, i64 s_l, i64 s_b, i64 B, i64 L) {
+  return seq != nullptr && s_l == 1 && aligned_to(seq, 16) && (B == 1 || (s_b >= L && (s_b * 4) % 16 == 0)) &&
+         (s_b * 4) < (1LL << 40);
+}
+
 bool seq_shape_ok(i64 B, i64 D, i64 L) {
   return B >= 1 && D >= 1 && L >= 8 && L % 8 == 0 && L < (1LL << 31) && D < (1LL << 31) && B < (1LL << 31);
 }
@@ -588,31 +799,34 @@ void seq_schedule(const DeviceInfo& dev, int nb, i64 B, i64 D, i64 L, Plan* plan
   plan->n_partials = B * nseg;
 }
 
-template <typename T, int W, bool SILU>
+template <typename T, int W, bool HAS_SEQ, bool SILU>
 cudaError_t seq_fwd_instance(SeqFwdParams* prm, const Plan* plan, cudaStream_t stream, int* nb_out) {
-  constexpr size_t smem = (size_t)seq_fwd_stages<T>() * seq_tile_bytes<T>() + 2 * seq_fwd_stages<T>() * sizeof(uint64_t);
+  constexpr size_t smem = (size_t)seq_fwd_stages<T>() * (seq_tile_bytes<T>() + (HAS_SEQ ? kIdsBytes : 0u)) +
+                          2 * seq_fwd_stages<T>() * sizeof(uint64_t);
   static std::atomic<uint64_t> attr{0};
   static std::atomic<int> occ{0};
   int nb = 1;
-  cudaError_t e = prepare(fwd_seq_tma_kernel<T, W, SILU>, smem, attr, occ, &nb);
+  cudaError_t e = prepare(fwd_seq_tma_kernel<T, W, HAS_SEQ, SILU>, smem, attr, occ, &nb);
   if (e != cudaSuccess) return e;
   if (nb_out) *nb_out = nb;
   if (prm == nullptr) return cudaSuccess;
-  return launch_pdl(fwd_seq_tma_kernel<T, W, SILU>, dim3((unsigned)plan->grid), dim3(kThreadsSeq), smem, stream, *prm);
+  return launch_pdl(fwd_seq_tma_kernel<T, W, HAS_SEQ, SILU>, dim3((unsigned)plan->grid), dim3(kThreadsSeq), smem,
+                    stream, *prm);
 }
 
-template <typename T, int W, bool SILU>
+template <typename T, int W, bool HAS_SEQ, bool SILU>
 cudaError_t seq_bwd_instance(SeqBwdParams* prm, const Plan* plan, cudaStream_t stream, int* nb_out) {
-  constexpr size_t smem =
-      (size_t)seq_bwd_stages<T>() * 2 * seq_tile_bytes<T>() + 2 * seq_bwd_stages<T>() * sizeof(uint64_t);
+  constexpr size_t smem = (size_t)seq_bwd_stages<T>() * (2 * seq_tile_bytes<T>() + (HAS_SEQ ? kIdsBytes : 0u)) +
+                          2 * seq_bwd_stages<T>() * sizeof(uint64_t);
   static std::atomic<uint64_t> attr{0};
   static std::atomic<int> occ{0};
   int nb = 1;
-  cudaError_t e = prepare(bwd_seq_tma_kernel<T, W, SILU>, smem, attr, occ, &nb);
+  cudaError_t e = prepare(bwd_seq_tma_kernel<T, W, HAS_SEQ, SILU>, smem, attr, occ, &nb);
   if (e != cudaSuccess) return e;
   if (nb_out) *nb_out = nb;
   if (prm == nullptr) return cudaSuccess;
-  return launch_pdl(bwd_seq_tma_kernel<T, W, SILU>, dim3((unsigned)plan->grid), dim3(kThreadsSeq), smem, stream, *prm);
+  return launch_pdl(bwd_seq_tma_kernel<T, W, HAS_SEQ, SILU>, dim3((unsigned)plan->grid), dim3(kThreadsSeq), smem,
+                    stream, *prm);
 }
 
 struct SeqFwdOp {
@@ -631,11 +845,17 @@ struct SeqFwdOp {
       storage.a.seg_len = plan->seg_len;
       storage.groups = plan->groups;
       if (!make_seq_map<T>(&storage.map_x, a.x, a.L, a.D, a.B, a.xs_c, a.xs_b)) return cudaErrorInvalidValue;
+      if (a.seq != nullptr && !make_ids_map(&storage.map_s, a.seq, a.L, a.B, a.ss_b)) return cudaErrorInvalidValue;
       prm = &storage;
     }
     int nb = 1;
-    cudaError_t e = silu ? seq_fwd_instance<T, W, true>(prm, plan, stream, &nb)
-                         : seq_fwd_instance<T, W, false>(prm, plan, stream, &nb);
+    cudaError_t e;
+    if (a.seq != nullptr)
+      e = silu ? seq_fwd_instance<T, W, true, true>(prm, plan, stream, &nb)
+               : seq_fwd_instance<T, W, true, false>(prm, plan, stream, &nb);
+    else
+      e = silu ? seq_fwd_instance<T, W, false, true>(prm, plan, stream, &nb)
+               : seq_fwd_instance<T, W, false, false>(prm, plan, stream, &nb);
     if (e != cudaSuccess || launch) return e;
     DeviceInfo dev;
     e = device_info(&dev);
@@ -664,11 +884,17 @@ struct SeqBwdOp {
       if (!make_seq_map<T>(&storage.map_x, a.x, a.L, a.D, a.B, a.xs_c, a.xs_b) ||
           !make_seq_map<T>(&storage.map_g, a.dout, a.L, a.D, a.B, a.gs_c, a.gs_b))
         return cudaErrorInvalidValue;
+      if (a.seq != nullptr && !make_ids_map(&storage.map_s, a.seq, a.L, a.B, a.ss_b)) return cudaErrorInvalidValue;
       prm = &storage;
     }
     int nb = 1;
-    cudaError_t e = silu ? seq_bwd_instance<T, W, true>(prm, plan, stream, &nb)
-                         : seq_bwd_instance<T, W, false>(prm, plan, stream, &nb);
+    cudaError_t e;
+    if (a.seq != nullptr)
+      e = silu ? seq_bwd_instance<T, W, true, true>(prm, plan, stream, &nb)
+               : seq_bwd_instance<T, W, true, false>(prm, plan, stream, &nb);
+    else
+      e = silu ? seq_bwd_instance<T, W, false, true>(prm, plan, stream, &nb)
+               : seq_bwd_instance<T, W, false, false>(prm, plan, stream, &nb);
     if (e != cudaSuccess || launch) return e;
     DeviceInfo dev;
     e = device_info(&dev);
@@ -682,14 +908,16 @@ struct SeqBwdOp {
 
 bool fwd_seq_tma_eligible(int dtype, const FwdArgs& a) {
   const int esz = esize(dtype);
-  return a.seq == nullptr && seq_shape_ok(a.B, a.D, a.L) && encode_fn() != nullptr &&
+  return (a.seq == nullptr || ids_ok(a.seq, a.ss_l, a.ss_b, a.B, a.L)) && seq_shape_ok(a.B, a.D, a.L) &&
+         encode_fn() != nullptr &&
          seq_tensor_ok(a.x, a.xs_c, a.xs_l, a.xs_b, a.B, a.D, esz) &&
          seq_tensor_ok(a.out, a.os_c, a.os_l, a.os_b, a.B, a.D, esz);
 }
 
 bool bwd_seq_tma_eligible(int dtype, const BwdArgs& a) {
   const int esz = esize(dtype);
-  return a.seq == nullptr && seq_shape_ok(a.B, a.D, a.L) && encode_fn() != nullptr &&
+  return (a.seq == nullptr || ids_ok(a.seq, a.ss_l, a.ss_b, a.B, a.L)) && seq_shape_ok(a.B, a.D, a.L) &&
+         encode_fn() != nullptr &&
          seq_tensor_ok(a.x, a.xs_c, a.xs_l, a.xs_b, a.B, a.D, esz) &&
          seq_tensor_ok(a.dout, a.gs_c, a.gs_l, a.gs_b, a.B, a.D, esz) &&
          seq_tensor_ok(a.dx, a.dxs_c, a.dxs_l, a.dxs_b, a.B, a.D, esz);

@@ -164,6 +164,31 @@ def test_seq_idx_vs_oracle(L, dtype, W, layout):
     _compare_oracle(x, w, b, seq, None, dout, None, W != 3, False, layout)
 
 
+@pytest.mark.parametrize("layout", ["contig", "chanlast"])
+@pytest.mark.parametrize("W", [2, 4])
+@pytest.mark.parametrize("dtype", ["fp32", "bf16"])
+def test_seq_idx_long_runs_vs_oracle(dtype, W, layout):
+    """Packed sequences much longer than a tile (the kernels' ungated path
+    for tiles without a boundary), a padding run, boundaries inside and at
+    the edges of tiles, and segment splits of long rows."""
+    dt = DTYPES[dtype]
+    B, D, L = 2, 48, 4096
+    seed = 91 + W
+    x = seeded((B, D, L), dt, seed)
+    w = seeded((D, W), dt, seed + 1, "uniform")
+    b = seeded((D,), dt, seed + 2, "uniform")
+    dout = seeded((B, D, L), dt, seed + 4)
+    runs = [[(1000, 0), (300, -1), (1, 1), (1259, 2), (1536, 3)], [(256, 0), (256, 1), (2048, 2), (1536, -1)]]
+    seq = torch.empty(B, L, dtype=torch.int32)
+    for r, row in enumerate(runs):
+        t = 0
+        for n, v in row:
+            seq[r, t:t + n] = v
+            t += n
+        assert t == L
+    _compare_oracle(x, w, b, seq, None, dout, None, True, False, layout)
+
+
 @pytest.mark.parametrize("W", [5, 6, 7, 8, 9])
 @pytest.mark.parametrize("layout", ["contig", "chanlast"])
 def test_wide_widths_vs_oracle(W, layout):
