@@ -275,6 +275,41 @@ def time_c2(args, world, rank, reducer):
     return dict(ms_per_step=total_ms / K, fwd_ms=fwd_ms, bwd_ms=bwd_ms, clocks=clk.summary())
 
 
+def gpu_local_cpus(dev_index):
+    """CPUs on the GPU's NUMA node (read from NVML; no setting is changed), or
+    None when NVML cannot tell."""
+    try:
+        import pynvml
+
+        props = torch.cuda.get_device_properties(dev_index)
+        bus = f"{props.pci_domain_id:08x}:{props.pci_bus_id:02x}:{props.pci_device_id:02x}.0"
+        pynvml.nvmlInit()
+        try:
+            h = pynvml.nvmlDeviceGetHandleByPciBusId(bus.encode())
+            words = pynvml.nvmlDeviceGetCpuAffinity(h, 64)
+        finally:
+            pynvml.nvmlShutdown()
+        cpus = {64 * i + j for i, w in enumerate(words) for j in range(64) if (w >> j) & 1}
+        cpus &= os.sched_getaffinity(0)
+        return cpus or None
+    except Exception:  # no NVML, no affinity information: leave placement alone
+        return None
+
+
+def pinned_near_gpu(tensors):
+    """Pinned host copies of `tensors`, first touched from the CPUs next to
+    the current GPU so that their pages sit on its NUMA node (the process's
+    CPU affinity is restored afterwards)."""
+    local = gpu_local_cpus(torch.cuda.current_device())
+    before = os.sched_getaffinity(0)
+    try:
+        if local:
+            os.sched_setaffinity(0, local)
+        return {k: (v.cpu() if v.is_cuda else v).pin_memory() for k, v in tensors.items()}
+    finally:
+        os.sched_setaffinity(0, before)
+
+
 def time_e2e(args, world, rank, reducer):
     """Public API, host buffers in and out, every step (three-stream
     pipeline: upload of step i+1 and download of step i overlap compute)."""
@@ -284,10 +319,10 @@ def time_e2e(args, world, rank, reducer):
     xd, wd, bd, initd, doutd = make_c2(99 + rank, "cuda")
     # Channel-last activations live on the host as (B, L, D) arrays.
     host = dict(x=xd.transpose(1, 2).contiguous(), w=wd, b=bd, init=initd, dout=doutd.transpose(1, 2).contiguous())
-    host = {k: v.cpu().pin_memory() for k, v in host.items()}
+    host = pinned_near_gpu(host)
     del xd, wd, bd, initd, doutd
-    outs = {k: torch.empty(s, dtype=DT).pin_memory() for k, s in dict(
-        out=(B, L, D), fs=(B, D, W - 1), dx=(B, L, D), dw=(D, W), db=(D,), dinit=(B, D, W - 1)).items()}
+    outs = pinned_near_gpu({k: torch.empty(s, dtype=DT) for k, s in dict(
+        out=(B, L, D), fs=(B, D, W - 1), dx=(B, L, D), dw=(D, W), db=(D,), dinit=(B, D, W - 1)).items()})
     h2d = sum(t.numel() * t.element_size() for t in host.values())
     d2h = sum(t.numel() * t.element_size() for t in outs.values())
     dev_in = [{k: torch.empty_like(v, device="cuda") for k, v in host.items()} for _ in range(2)]
