@@ -18,8 +18,11 @@
 // Semantics are those of cc1d_fwd.cu / cc1d_bwd.cu (reference CPU kernels
 // src/causal_conv1d_mojo/fwd_cpu/kernel.mojo:64-117,
 // bwd_full_cpu/kernel.mojo:26-314; final/initial states as
-// src/causal_conv1d_mojo/reference.py:50-56).  seq_idx calls use the
-// register-streaming kernels.
+// src/causal_conv1d_mojo/reference.py:50-56).
+//
+// Rows whose pitch is not a multiple of 16 bytes (odd lengths of contiguous
+// tensors) take the "shifted" kernels below, which stream the same tiles
+// through a 2-D view of the tensor laid on its own 16-byte grid.
 #include <cudaTypedefs.h>
 
 #include <type_traits>
@@ -56,6 +59,9 @@ namespace {
 #ifndef CC1D_SEQ_BWD_IDS_MIN_BLOCKS
 #define CC1D_SEQ_BWD_IDS_MIN_BLOCKS 3  // with seq_idx (174 registers uncapped: 2 blocks per SM)
 #endif
+#ifndef CC1D_SEQ_BWD_SH_MIN_BLOCKS
+#define CC1D_SEQ_BWD_SH_MIN_BLOCKS 3  // shifted rows (4 spills ~200 bytes at W = 4)
+#endif
 
 constexpr int kSW = CC1D_SEQ_WARPS;  // consumer warps
 constexpr int kRows = 2 * kSW;       // channel rows per tile
@@ -78,11 +84,25 @@ constexpr int seq_bwd_stages() {
 // Bytes of a stage's sequence-id tile (kTL int32 ids), present with seq_idx.
 constexpr unsigned kIdsBytes = kTL * sizeof(int);
 
+// Shifted-row geometry (rows whose pitch is not a multiple of 16 bytes):
+// the tensor viewed as rows of `in` elements; a row tile is one box of
+// `rows` such rows starting at the one that holds the tile's first element.
+struct ShiftGeom {
+  int in;        // elements per view row (a power of two, 16..128 bytes)
+  int in_log2;
+  int rows;      // kTL / in + 1
+  unsigned tx;   // bytes one tensor's tile delivers (kRows boxes)
+  // Tiles of a segment: seg_len / kTL, and for a row's last segment enough
+  // to reach L from its start - (E - 1).  Counted on the host.
+  int tiles_full, tiles_last;
+};
+
 struct alignas(64) SeqFwdParams {
   CUtensorMap map_x;
   CUtensorMap map_s;  // seq_idx as (L, 1, B) int32, when given
   FwdArgs a;
   i64 groups;
+  ShiftGeom sg;
 };
 struct alignas(64) SeqBwdParams {
   CUtensorMap map_x;
@@ -90,6 +110,7 @@ struct alignas(64) SeqBwdParams {
   CUtensorMap map_s;
   BwdArgs a;
   i64 groups;
+  ShiftGeom sg;
 };
 
 // The 8 sequence ids [8*lane, 8*lane+8) of a stage's id tile.
@@ -674,6 +695,508 @@ __global__ void __launch_bounds__(kThreadsSeq, W > 5 ? 1 : (HAS_SEQ ? CC1D_SEQ_B
 }
 
 // ---------------------------------------------------------------------------
+// Rows whose pitch is not a multiple of 16 bytes ("shifted" rows)
+// ---------------------------------------------------------------------------
+// TMA cannot describe such rows with a 3-D map (strides must be multiples of
+// 16 bytes).  The tensor is then viewed as a 2-D array of view rows of `in`
+// elements (the largest power of two of at most 128 bytes that divides the
+// tensor's extent), and the tiles of a channel row are laid on the tensor's
+// own 16-byte grid instead of on the row's start: with off = the offset of
+// the row's position 0 in its 16-byte unit (0 .. E-1, E = 16 / sizeof(T)),
+// the row's tiles begin at positions seg_start - off + 256 j.  Every lane's
+// 8 elements are then one aligned vector, in shared memory and in global
+// memory, and nothing is realigned.  A tile is one box of kTL / in + 1 view
+// rows starting at the view row that holds the tile's first element, which
+// sits o2 (a multiple of E) elements into the box.
+//
+// The first tile of a row holds, at positions -off .. -1, the end of the
+// previous row: lane 0 overwrites those elements in shared memory with xc
+// there (initial states or zeros); outputs there are not stored and dpre
+// there is 0.  Past L a tile holds the next row: stores are masked and dpre
+// is 0.  Segment bounds move with the row (seg_start - off), so segments
+// still partition the row; the two rows of a warp, whose offsets differ,
+// share every lane's frame index and keep their own positions.
+
+// Largest view row, in bytes.  A box is kTL * sizeof(T) + (view row) bytes.
+constexpr int kShMaxRowBytes = 128;
+
+template <typename T>
+constexpr int unit_elems() {
+  return 16 / (int)sizeof(T);
+}
+// smem bytes of one shifted row tile: the largest box.
+template <typename T>
+constexpr unsigned sh_row_bytes() {
+  return ((unsigned)(kTL * sizeof(T) + kShMaxRowBytes) + 127u) / 128u * 128u;  // 640 or 1152
+}
+
+// xc (x preceded by initial_states or zeros) of one row at position q.
+template <typename T>
+__device__ __forceinline__ float xc_one(const T* x, i64 xs_l, const T* init, i64 is_l, int H, int q) {
+  if (q >= 0) return Cvt<T>::f(x[q * xs_l]);
+  if (init != nullptr && q >= -H) return Cvt<T>::f(init[(q + H) * is_l]);
+  return 0.f;
+}
+
+// xc of rows (ra, ra + 1) at their own positions qa, qb.
+template <typename T>
+__device__ __forceinline__ float2 xc_rows(const T* x, i64 xs_c, i64 xs_l, const T* init, i64 is_c, i64 is_l, int H,
+                                          int qa, int qb, bool va, bool vb) {
+  return f2(va ? xc_one(x, xs_l, init, is_l, H, qa) : 0.f,
+            vb ? xc_one(x + xs_c, xs_l, init != nullptr ? init + is_c : nullptr, is_l, H, qb) : 0.f);
+}
+
+// The 8 elements [8*lane, 8*lane+8) of a row tile that starts at `row`
+// (16-byte aligned), as floats.
+template <typename T>
+__device__ __forceinline__ void lds8_row(const unsigned char* row, int lane, float (&v)[8]) {
+  const T* p = reinterpret_cast<const T*>(row) + lane * 8;
+  if constexpr (sizeof(T) == 2) {
+    const uint4 u = *reinterpret_cast<const uint4*>(p);
+    const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float2 f = Pair<T>::unpack(w[i]);
+      v[2 * i] = f.x;
+      v[2 * i + 1] = f.y;
+    }
+  } else {
+    const float4 a = reinterpret_cast<const float4*>(p)[0];
+    const float4 b = reinterpret_cast<const float4*>(p)[1];
+    v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
+    v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+  }
+}
+
+// Stores a lane's 8 values at row positions [q, q + 8) (q + row start on the
+// 16-byte grid): one vector when all lie in [0, L), else the ones that do.
+template <typename T>
+__device__ __forceinline__ void stg8_rowpos(T* row, int q, int L, const float (&v)[8]) {
+  if (q >= 0 && q + 8 <= L) {
+    stg8<T>(row + q, v);
+  } else {
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+      if (q + i >= 0 && q + i < L) row[q + i] = Cvt<T>::to(v[i]);
+  }
+}
+
+// First tile of a row: its positions -off .. -1 hold the previous row's
+// elements; lane 0 overwrites them in shared memory with xc there (initial
+// states or zeros).  The caller orders these writes before the stage's next
+// TMA with a proxy fence.
+template <typename T>
+__device__ __forceinline__ void fix_row_head(unsigned char* row, int off, const T* init, i64 is_l, int H) {
+  T* e = reinterpret_cast<T*>(row);
+  for (int i = 0; i < off; ++i) {
+    const int q = i - off;
+    e[i] = (init != nullptr && q >= -H) ? init[(q + H) * is_l] : Cvt<T>::to(0.f);
+  }
+}
+
+// Producer: one box per channel row of the group, at the view row holding
+// the row's first tile element (rows past D read whatever lies there or the
+// fill value; nothing is stored for them).
+__device__ __forceinline__ void shift_load_rows(unsigned char* dst, unsigned row_bytes, const CUtensorMap* map,
+                                                uint64_t* bar, i64 rbase, i64 s_c, int t, int E, int in_log2) {
+#pragma unroll 1
+  for (int r = 0; r < kRows; ++r) {
+    const i64 e0 = ((rbase + r * s_c) & ~(i64)(E - 1)) + t;
+    tma_load_3d(dst + r * row_bytes, map, bar, 0, (int)(e0 >> in_log2), 0);
+  }
+}
+
+template <typename T, int W, bool SILU>
+__global__ void __launch_bounds__(kThreadsSeq, CC1D_SEQ_FWD_MIN_BLOCKS) fwd_shift_tma_kernel(const __grid_constant__ SeqFwdParams p) {
+  constexpr int H = W - 1;
+  constexpr int E = unit_elems<T>();
+  constexpr unsigned RB = sh_row_bytes<T>();
+  constexpr unsigned SB = kRows * RB;
+  constexpr int NS = seq_fwd_stages<T>();
+  extern __shared__ __align__(128) unsigned char smem[];
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + NS * SB);
+  uint64_t* empty = full + NS;
+  const FwdArgs& a = p.a;
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const i64 item = blockIdx.x;
+  const i64 seg = item % a.nseg;
+  const i64 rest = item / a.nseg;
+  const i64 grp = rest % p.groups;
+  const i64 b = rest / p.groups;
+  const i64 c0 = grp * kRows;
+  // Positions fit 32 bits (L < 2^31 - 2^12).
+  const int L = (int)a.L, seg_len = (int)a.seg_len;
+  const int t0 = (int)seg * seg_len;
+  const bool last_seg = seg == a.nseg - 1;
+  const int ntiles = last_seg ? p.sg.tiles_last : p.sg.tiles_full;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < NS; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], kSW);
+    }
+    fence_mbar_init();
+  }
+  __syncthreads();
+  griddep_wait();  // inputs of this launch may come from the previous kernel
+  griddep_launch_dependents();
+
+  if (warp == kSW) {
+    if (lane == 0) {
+      prefetch_tensormap(&p.map_x);
+      const i64 rbase = b * a.xs_b + c0 * a.xs_c;
+      for (int k = 0; k < ntiles; ++k) {
+        const unsigned s = k % NS, use = k / NS;
+        if (use > 0 && !mbar_wait(&empty[s], (use - 1) & 1)) return;
+        mbar_arrive_expect_tx(&full[s], p.sg.tx);
+        shift_load_rows(smem + s * SB, RB, &p.map_x, &full[s], rbase, a.xs_c, t0 + k * kTL, E, p.sg.in_log2);
+      }
+    }
+    return;
+  }
+
+  const i64 ra = c0 + 2 * warp;  // rows (channels) of this warp: ra, ra + 1
+  const bool va = ra < a.D, vb = ra + 1 < a.D;
+  const T* __restrict__ wt = static_cast<const T*>(a.w);
+  const T* __restrict__ bias = static_cast<const T*>(a.bias);
+  float2 wp[W];
+#pragma unroll
+  for (int k = 0; k < W; ++k)
+    wp[k] = f2(va ? Cvt<T>::f(wt[ra * a.ws_c + k * a.ws_k]) : 0.f, vb ? Cvt<T>::f(wt[(ra + 1) * a.ws_c + k * a.ws_k]) : 0.f);
+  const float2 bp = f2((bias && va) ? Cvt<T>::f(bias[ra * a.bs]) : 0.f, (bias && vb) ? Cvt<T>::f(bias[(ra + 1) * a.bs]) : 0.f);
+  const i64 Ra = b * a.xs_b + ra * a.xs_c, Rb = Ra + a.xs_c;  // element index of each row's position 0
+  const int off_a = (int)(Ra & (E - 1)), off_b = (int)(Rb & (E - 1));
+  const unsigned o2a = (unsigned)((Ra & (p.sg.in - 1)) - off_a) * sizeof(T);
+  const unsigned o2b = (unsigned)((Rb & (p.sg.in - 1)) - off_b) * sizeof(T);
+  const T* __restrict__ xr = static_cast<const T*>(a.x) + Ra;
+  const T* __restrict__ ir = a.init ? static_cast<const T*>(a.init) + b * a.is_b + ra * a.is_c : nullptr;
+  T* __restrict__ oa = static_cast<T*>(a.out) + Ra;  // out has x's strides
+  T* __restrict__ ob = oa + a.xs_c;
+  // Row positions of this lane's element 0 in the segment's first tile.
+  const int qa0 = t0 - off_a + 8 * lane, qb0 = t0 - off_b + 8 * lane;
+
+  // Halo of lane 0 in the first tile: xc before each row's first tile.
+  float2 carry[H];
+#pragma unroll
+  for (int j = 0; j < H; ++j)
+    carry[j] = xc_rows(xr, a.xs_c, a.xs_l, ir, a.is_c, a.is_l, H, t0 - off_a - H + j, t0 - off_b - H + j, va, vb);
+
+  for (int k = 0; k < ntiles; ++k) {
+    const unsigned s = k % NS, use = k / NS;
+    if (!mbar_wait(&full[s], use & 1)) return;
+    unsigned char* rowa = smem + s * SB + (2 * warp) * RB + o2a;
+    unsigned char* rowb = smem + s * SB + (2 * warp + 1) * RB + o2b;
+    if (t0 == 0 && k == 0) {
+      if (lane == 0) {
+        if (va) fix_row_head<T>(rowa, off_a, ir, a.is_l, H);
+        if (vb) fix_row_head<T>(rowb, off_b, ir != nullptr ? ir + a.is_c : nullptr, a.is_l, H);
+        fence_proxy_async_smem();
+      }
+      __syncwarp();
+    }
+    float xa[8], xb[8];
+    lds8_row<T>(rowa, lane, xa);
+    lds8_row<T>(rowb, lane, xb);
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[s]);
+    const int qa = qa0 + k * kTL, qb = qb0 + k * kTL;
+    float2 xp[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) xp[i] = f2(xa[i], xb[i]);
+    float2 h[H];
+#pragma unroll
+    for (int j = 0; j < H; ++j) {
+      const float2 up = shfl_up2(xp[8 - H + j], 1);
+      const float2 nc = shfl2(xp[8 - H + j], 31);
+      h[j] = lane == 0 ? carry[j] : up;
+      carry[j] = nc;
+    }
+    float oa8[8], ob8[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      float2 acc = bp;
+#pragma unroll
+      for (int kk = 0; kk < W; ++kk) {
+        const int q = i - H + kk;
+        acc = fma2(wp[kk], q >= 0 ? xp[q >= 0 ? q : 0] : h[q >= 0 ? 0 : q + H], acc);
+      }
+      if (SILU) acc = silu2(acc);
+      oa8[i] = acc.x;
+      ob8[i] = acc.y;
+    }
+    if (va) stg8_rowpos<T>(oa, qa, L, oa8);
+    if (vb) stg8_rowpos<T>(ob, qb, L, ob8);
+  }
+  if (a.fin != nullptr && last_seg && lane < H) {
+    T* f = static_cast<T*>(a.fin) + b * a.fs_b + ra * a.fs_c + lane * a.fs_l;
+    const i64 q = a.L - H + lane;
+    const float2 v = xc_pair(xr, a.xs_c, a.xs_l, ir, a.is_c, a.is_l, H, q, va, vb);
+    if (va) f[0] = Cvt<T>::to(v.x);
+    if (vb) f[a.fs_c] = Cvt<T>::to(v.y);
+  }
+}
+
+// dpre of rows (ra, ra + 1) at their own positions qa, qb (0 at or past L).
+template <typename T, int W, bool SILU>
+__device__ __forceinline__ float2 dpre_rows(const T* xr, const T* gr, const T* ir, const BwdArgs& a,
+                                            const float2 (&wp)[W], float2 bp, int qa, int qb, bool va, bool vb) {
+  constexpr int H = W - 1;
+  const bool ia = va && qa < (int)a.L, ib = vb && qb < (int)a.L;  // nothing is read past the row
+  float2 pre = bp;
+#pragma unroll
+  for (int kk = 0; kk < W; ++kk)
+    pre = fma2(wp[kk], xc_rows(xr, a.xs_c, a.xs_l, ir, a.is_c, a.is_l, H, qa - H + kk, qb - H + kk, ia, ib), pre);
+  const float2 g = f2(ia ? Cvt<T>::f(gr[qa]) : 0.f, ib ? Cvt<T>::f(gr[a.xs_c + qb]) : 0.f);
+  return SILU ? mul2(g, silu_grad2(pre)) : g;
+}
+
+// dx of a lane's 8 positions (rows at qa, qb) from dpre of those positions
+// (d) and of the H positions after them (rh), plus dfinal where final_states
+// read them; stored within [0, L).
+template <typename T, int W>
+__device__ __forceinline__ void emit_dx_shift(const float2 (&d)[8], const float2 (&rh)[W - 1], const float2 (&wp)[W],
+                                              int qa, int qb, int L, const BwdArgs& a, T* dxa, const T* fa, bool va,
+                                              bool vb) {
+  constexpr int H = W - 1;
+  float ea[8], eb[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    float2 acc = f2(0.f, 0.f);
+#pragma unroll
+    for (int m = 0; m <= H; ++m) {
+      const int q = i + m;
+      acc = fma2(wp[H - m], q < 8 ? d[q < 8 ? q : 0] : rh[q < 8 ? 0 : q - 8], acc);
+    }
+    ea[i] = acc.x;
+    eb[i] = acc.y;
+  }
+  if (fa != nullptr && (qa + 8 + H > L || qb + 8 + H > L)) {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const int fqa = qa + i + H - L, fqb = qb + i + H - L;
+      if (va && fqa >= 0 && qa + i < L) ea[i] += Cvt<T>::f(fa[fqa * a.fs_l]);
+      if (vb && fqb >= 0 && qb + i < L) eb[i] += Cvt<T>::f(fa[a.fs_c + fqb * a.fs_l]);
+    }
+  }
+  if (va) stg8_rowpos<T>(dxa, qa, L, ea);
+  if (vb) stg8_rowpos<T>(dxa + a.xs_c, qb, L, eb);
+}
+
+template <typename T, int W, bool SILU>
+__global__ void __launch_bounds__(kThreadsSeq, W > 5 ? 1 : CC1D_SEQ_BWD_SH_MIN_BLOCKS) bwd_shift_tma_kernel(const __grid_constant__ SeqBwdParams p) {
+  constexpr int H = W - 1;
+  constexpr int E = unit_elems<T>();
+  constexpr unsigned RB = sh_row_bytes<T>();
+  constexpr unsigned TB = kRows * RB;
+  constexpr unsigned SB = 2 * TB;
+  constexpr int NS = seq_bwd_stages<T>();
+  extern __shared__ __align__(128) unsigned char smem[];
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + NS * SB);
+  uint64_t* empty = full + NS;
+  const BwdArgs& a = p.a;
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const i64 item = blockIdx.x;
+  const i64 seg = item % a.nseg;
+  const i64 rest = item / a.nseg;
+  const i64 grp = rest % p.groups;
+  const i64 b = rest / p.groups;
+  const i64 c0 = grp * kRows;
+  const int L = (int)a.L, seg_len = (int)a.seg_len;
+  const int t0 = (int)seg * seg_len;
+  const bool last_seg = seg == a.nseg - 1;
+  const int ntiles = last_seg ? p.sg.tiles_last : p.sg.tiles_full;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < NS; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], kSW);
+    }
+    fence_mbar_init();
+  }
+  __syncthreads();
+  griddep_wait();
+  griddep_launch_dependents();
+
+  if (warp == kSW) {
+    if (lane == 0) {
+      prefetch_tensormap(&p.map_x);
+      prefetch_tensormap(&p.map_g);
+      const i64 rbase = b * a.xs_b + c0 * a.xs_c;  // dout and dx have x's strides
+      for (int k = 0; k < ntiles; ++k) {
+        const unsigned s = k % NS, use = k / NS;
+        if (use > 0 && !mbar_wait(&empty[s], (use - 1) & 1)) return;
+        mbar_arrive_expect_tx(&full[s], 2 * p.sg.tx);
+        const int t = t0 + k * kTL;
+        shift_load_rows(smem + s * SB, RB, &p.map_x, &full[s], rbase, a.xs_c, t, E, p.sg.in_log2);
+        shift_load_rows(smem + s * SB + TB, RB, &p.map_g, &full[s], rbase, a.xs_c, t, E, p.sg.in_log2);
+      }
+    }
+    return;
+  }
+
+  const i64 ra = c0 + 2 * warp;
+  const bool va = ra < a.D, vb = ra + 1 < a.D;
+  const T* __restrict__ wt = static_cast<const T*>(a.w);
+  const T* __restrict__ bias = static_cast<const T*>(a.bias);
+  float2 wp[W];
+#pragma unroll
+  for (int k = 0; k < W; ++k)
+    wp[k] = f2(va ? Cvt<T>::f(wt[ra * a.ws_c + k * a.ws_k]) : 0.f, vb ? Cvt<T>::f(wt[(ra + 1) * a.ws_c + k * a.ws_k]) : 0.f);
+  const float2 bp = f2((bias && va) ? Cvt<T>::f(bias[ra * a.bs]) : 0.f, (bias && vb) ? Cvt<T>::f(bias[(ra + 1) * a.bs]) : 0.f);
+  const i64 Ra = b * a.xs_b + ra * a.xs_c, Rb = Ra + a.xs_c;
+  const int off_a = (int)(Ra & (E - 1)), off_b = (int)(Rb & (E - 1));
+  const unsigned o2a = (unsigned)((Ra & (p.sg.in - 1)) - off_a) * sizeof(T);
+  const unsigned o2b = (unsigned)((Rb & (p.sg.in - 1)) - off_b) * sizeof(T);
+  const T* __restrict__ xr = static_cast<const T*>(a.x) + Ra;
+  const T* __restrict__ gr = static_cast<const T*>(a.dout) + Ra;
+  const T* __restrict__ ir = a.init ? static_cast<const T*>(a.init) + b * a.is_b + ra * a.is_c : nullptr;
+  T* __restrict__ dxa = static_cast<T*>(a.dx) + Ra;
+  const T* __restrict__ fa = a.dfin ? static_cast<const T*>(a.dfin) + b * a.fs_b + ra * a.fs_c : nullptr;
+  const int qa0 = t0 - off_a + 8 * lane, qb0 = t0 - off_b + 8 * lane;
+
+  float2 carry[H];
+#pragma unroll
+  for (int j = 0; j < H; ++j)
+    carry[j] = xc_rows(xr, a.xs_c, a.xs_l, ir, a.is_c, a.is_l, H, t0 - off_a - H + j, t0 - off_b - H + j, va, vb);
+  // dpre just past each row's segment (0 past the row), for lane 31's last dx.
+  float2 rend[H];
+  {
+    const int ea = last_seg ? L : t0 + seg_len - off_a, eb = last_seg ? L : t0 + seg_len - off_b;
+#pragma unroll
+    for (int j = 0; j < H; ++j) rend[j] = dpre_rows<T, W, SILU>(xr, gr, ir, a, wp, bp, ea + j, eb + j, va, vb);
+  }
+  // dinitial_states from dpre of positions 0 .. H-1, read directly.
+  if (t0 == 0 && a.dinit != nullptr) {
+    float2 dq[H];
+#pragma unroll
+    for (int i = 0; i < H; ++i) dq[i] = dpre_rows<T, W, SILU>(xr, gr, ir, a, wp, bp, i, i, va, vb);
+    if (lane == 0) {
+      T* di = static_cast<T*>(a.dinit) + b * a.dis_b + ra * a.dis_c;
+#pragma unroll
+      for (int i = 0; i < H; ++i) {
+        float2 acc = f2(0.f, 0.f);
+#pragma unroll
+        for (int kk = 0; kk <= i; ++kk) acc = fma2(wp[kk], dq[i - kk], acc);
+        if (fa != nullptr && i - L >= 0) {
+          if (va) acc.x += Cvt<T>::f(fa[(i - L) * a.fs_l]);
+          if (vb) acc.y += Cvt<T>::f(fa[a.fs_c + (i - L) * a.fs_l]);
+        }
+        if (va) di[i * a.dis_l] = Cvt<T>::to(acc.x);
+        if (vb) di[a.dis_c + i * a.dis_l] = Cvt<T>::to(acc.y);
+      }
+    }
+  }
+
+  float2 dw[W];
+#pragma unroll
+  for (int k = 0; k < W; ++k) dw[k] = f2(0.f, 0.f);
+  float2 db = f2(0.f, 0.f);
+  float2 dprev[8];
+  int qpa = 0, qpb = 0;  // row positions of dprev's element 0
+
+  for (int k = 0; k < ntiles; ++k) {
+    const unsigned s = k % NS, use = k / NS;
+    if (!mbar_wait(&full[s], use & 1)) return;
+    unsigned char* rowa = smem + s * SB + (2 * warp) * RB + o2a;
+    unsigned char* rowb = smem + s * SB + (2 * warp + 1) * RB + o2b;
+    if (t0 == 0 && k == 0) {
+      if (lane == 0) {
+        if (va) fix_row_head<T>(rowa, off_a, ir, a.is_l, H);
+        if (vb) fix_row_head<T>(rowb, off_b, ir != nullptr ? ir + a.is_c : nullptr, a.is_l, H);
+        fence_proxy_async_smem();
+      }
+      __syncwarp();
+    }
+    float xa[8], xb[8], ga[8], gb[8];
+    lds8_row<T>(rowa, lane, xa);
+    lds8_row<T>(rowb, lane, xb);
+    lds8_row<T>(rowa + TB, lane, ga);
+    lds8_row<T>(rowb + TB, lane, gb);
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[s]);
+    const int qa = qa0 + k * kTL, qb = qb0 + k * kTL;
+    float2 xp[8], d[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) xp[i] = f2(xa[i], xb[i]);
+    float2 h[H];
+#pragma unroll
+    for (int j = 0; j < H; ++j) {
+      const float2 up = shfl_up2(xp[8 - H + j], 1);
+      const float2 nc = shfl2(xp[8 - H + j], 31);
+      h[j] = lane == 0 ? carry[j] : up;
+      carry[j] = nc;
+    }
+    const bool edge = qa < 0 || qb < 0 || qa + 8 > L || qb + 8 > L;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      float2 pre = bp;
+#pragma unroll
+      for (int kk = 0; kk < W; ++kk) {
+        const int q = i - H + kk;
+        pre = fma2(wp[kk], q >= 0 ? xp[q >= 0 ? q : 0] : h[q >= 0 ? 0 : q + H], pre);
+      }
+      const float2 g = f2(ga[i], gb[i]);
+      d[i] = SILU ? mul2(g, silu_grad2(pre)) : g;
+      if (edge) {
+        // Outside the row: the neighbouring rows' elements carry no gradient.
+        if (qa + i < 0 || qa + i >= L) d[i].x = 0.f;
+        if (qb + i < 0 || qb + i >= L) d[i].y = 0.f;
+      }
+      db = add2(db, d[i]);
+#pragma unroll
+      for (int kk = 0; kk < W; ++kk) {
+        const int q = i - H + kk;
+        dw[kk] = fma2(d[i], q >= 0 ? xp[q >= 0 ? q : 0] : h[q >= 0 ? 0 : q + H], dw[kk]);
+      }
+    }
+    // dx of the previous tile: lane 31 now has its right halo.
+    if (k > 0) {
+      float2 rh[H];
+#pragma unroll
+      for (int j = 0; j < H; ++j) {
+        const float2 nxt = shfl_down2(dprev[j], 1);
+        const float2 first = shfl2(d[j], 0);
+        rh[j] = lane == 31 ? first : nxt;
+      }
+      emit_dx_shift<T, W>(dprev, rh, wp, qpa, qpb, L, a, dxa, fa, va, vb);
+    }
+#pragma unroll
+    for (int i = 0; i < 8; ++i) dprev[i] = d[i];
+    qpa = qa;
+    qpb = qb;
+  }
+  if (ntiles > 0) {
+    float2 rh[H];
+#pragma unroll
+    for (int j = 0; j < H; ++j) {
+      const float2 nxt = shfl_down2(dprev[j], 1);
+      rh[j] = lane == 31 ? rend[j] : nxt;
+    }
+    emit_dx_shift<T, W>(dprev, rh, wp, qpa, qpb, L, a, dxa, fa, va, vb);
+  }
+  // Warp sums of the dweight / dbias partials; lane 0 writes this item's slot.
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) {
+#pragma unroll
+    for (int kk = 0; kk < W; ++kk) dw[kk] = add2(dw[kk], shfl_down2(dw[kk], off));
+    db = add2(db, shfl_down2(db, off));
+  }
+  if (lane == 0) {
+    float* pp = a.partials + ((b * a.nseg + seg) * a.D + ra) * (W + 1);
+    if (va) {
+#pragma unroll
+      for (int kk = 0; kk < W; ++kk) pp[kk] = dw[kk].x;
+      pp[W] = db.x;
+    }
+    if (vb) {
+#pragma unroll
+      for (int kk = 0; kk < W; ++kk) pp[W + 1 + kk] = dw[kk].y;
+      pp[2 * W + 1] = db.y;
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
 // Host side
 // ---------------------------------------------------------------------------
 
@@ -759,6 +1282,88 @@ bool seq_shape_ok(i64 B, i64 D, i64 L) {
   return B >= 1 && D >= 1 && L >= 8 && L % 8 == 0 && L < (1LL << 31) && D < (1LL << 31) && B < (1LL << 31);
 }
 
+// Elements from the base of a (B, D, L) tensor with unit seqlen stride to
+// the end of its last row.
+i64 sh_extent(i64 B, i64 D, i64 L, i64 s_c, i64 s_b) { return (B - 1) * s_b + (D - 1) * s_c + L; }
+
+// View-row geometry for a tensor extent: rows of the largest power of two
+// elements, 16 .. kShMaxRowBytes bytes, that divides the extent (sh_ok
+// guarantees 16 bytes does); and the tile counts of the segments.
+template <typename T>
+ShiftGeom sh_geom(i64 extent, i64 L, i64 nseg, i64 seg_len) {
+  ShiftGeom g;
+  g.tiles_full = (int)(seg_len / kTL);
+  g.tiles_last = (int)ceil_div(L - (nseg - 1) * seg_len + unit_elems<T>() - 1, (i64)kTL);
+  int in = kShMaxRowBytes / (int)sizeof(T);
+  while (in > unit_elems<T>() && extent % in != 0) in >>= 1;
+  g.in = in;
+  g.in_log2 = 0;
+  while ((1 << g.in_log2) < in) ++g.in_log2;
+  g.rows = kTL / in + 1;
+  g.tx = (unsigned)(kRows * g.rows * in * (int)sizeof(T));
+  return g;
+}
+
+// The tensor as (in, extent / in, 1) view rows; box (in, kTL / in + 1, 1).
+template <typename T>
+bool make_sh_map(CUtensorMap* m, const void* base, i64 extent, const ShiftGeom& g) {
+  PFN_cuTensorMapEncodeTiled_v12000 enc = encode_fn();
+  if (enc == nullptr) return false;
+  const i64 units = extent / g.in;
+  const i64 rb = (i64)g.in * (i64)sizeof(T);
+  cuuint64_t dims[3] = {(cuuint64_t)g.in, (cuuint64_t)units, 1};
+  cuuint64_t strides[2] = {(cuuint64_t)rb, (cuuint64_t)(units * rb)};
+  cuuint32_t box[3] = {(cuuint32_t)g.in, (cuuint32_t)g.rows, 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  const CUresult r = enc(m, tma_dtype<T>(), 3, const_cast<void*>(base), dims, strides, box, estr,
+                         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    set_error_detail("cuTensorMapEncodeTiled returned %d (shifted rows, %lld view rows)", (int)r, (long long)units);
+  return r == CUDA_SUCCESS;
+}
+
+// Rows with unit seqlen stride, every tensor 16-byte aligned, with the SAME
+// strides (so one offset per row serves all of them), non-overlapping rows,
+// and an extent that is a whole number of 16-byte units addressable by
+// 32-bit view-row indices.
+bool sh_ok(const void* base, i64 s_c, i64 s_l, i64 s_b, i64 B, i64 D, i64 L, int esz) {
+  const i64 E = 16 / esz;
+  const i64 ext = sh_extent(B, D, L, s_c, s_b);
+  return base != nullptr && s_l == 1 && aligned_to(base, 16) && (D == 1 || s_c >= L) &&
+         (B == 1 || s_b >= (D - 1) * s_c + L) && ext % E == 0 && (ext + 8 * s_c + 2 * kTL) / E < (1LL << 31);
+}
+
+// Shifted tiles: any L >= 8 (stores are masked at the row end); positions
+// (-8 .. L + 2 tiles) are 32-bit in the kernels.
+bool sh_shape_ok(i64 B, i64 D, i64 L) {
+  return B >= 1 && D >= 1 && L >= 8 && L < (1LL << 31) - 4096 && D < (1LL << 31) && B < (1LL << 31);
+}
+
+// The shifted kernels take rows the 3-D maps cannot describe, without
+// seq_idx (those take the register kernels).
+bool fwd_shifted(size_t esz, const FwdArgs& a) {
+  const int e = (int)esz;
+  if (a.seq != nullptr || !sh_shape_ok(a.B, a.D, a.L)) return false;
+  if (seq_shape_ok(a.B, a.D, a.L) && seq_tensor_ok(a.x, a.xs_c, a.xs_l, a.xs_b, a.B, a.D, e) &&
+      seq_tensor_ok(a.out, a.os_c, a.os_l, a.os_b, a.B, a.D, e))
+    return false;  // the 3-D maps apply
+  return a.os_c == a.xs_c && a.os_b == a.xs_b && sh_ok(a.x, a.xs_c, a.xs_l, a.xs_b, a.B, a.D, a.L, e) &&
+         sh_ok(a.out, a.os_c, a.os_l, a.os_b, a.B, a.D, a.L, e);
+}
+
+bool bwd_shifted(size_t esz, const BwdArgs& a) {
+  const int e = (int)esz;
+  if (a.seq != nullptr || !sh_shape_ok(a.B, a.D, a.L)) return false;
+  if (seq_shape_ok(a.B, a.D, a.L) && seq_tensor_ok(a.x, a.xs_c, a.xs_l, a.xs_b, a.B, a.D, e) &&
+      seq_tensor_ok(a.dout, a.gs_c, a.gs_l, a.gs_b, a.B, a.D, e) &&
+      seq_tensor_ok(a.dx, a.dxs_c, a.dxs_l, a.dxs_b, a.B, a.D, e))
+    return false;
+  return a.gs_c == a.xs_c && a.gs_b == a.xs_b && a.dxs_c == a.xs_c && a.dxs_b == a.xs_b &&
+         sh_ok(a.x, a.xs_c, a.xs_l, a.xs_b, a.B, a.D, a.L, e) && sh_ok(a.dout, a.gs_c, a.gs_l, a.gs_b, a.B, a.D, a.L, e) &&
+         sh_ok(a.dx, a.dxs_c, a.dxs_l, a.dxs_b, a.B, a.D, a.L, e);
+}
+
 int esize(int dtype) { return dtype == 2 ? 4 : 2; }
 
 template <typename K>
@@ -829,6 +1434,36 @@ cudaError_t seq_bwd_instance(SeqBwdParams* prm, const Plan* plan, cudaStream_t s
                     stream, *prm);
 }
 
+template <typename T, int W, bool SILU>
+cudaError_t shift_fwd_instance(SeqFwdParams* prm, const Plan* plan, cudaStream_t stream, int* nb_out) {
+  constexpr size_t smem =
+      (size_t)seq_fwd_stages<T>() * kRows * sh_row_bytes<T>() + 2 * seq_fwd_stages<T>() * sizeof(uint64_t);
+  static std::atomic<uint64_t> attr{0};
+  static std::atomic<int> occ{0};
+  int nb = 1;
+  cudaError_t e = prepare(fwd_shift_tma_kernel<T, W, SILU>, smem, attr, occ, &nb);
+  if (e != cudaSuccess) return e;
+  if (nb_out) *nb_out = nb;
+  if (prm == nullptr) return cudaSuccess;
+  return launch_pdl(fwd_shift_tma_kernel<T, W, SILU>, dim3((unsigned)plan->grid), dim3(kThreadsSeq), smem, stream,
+                    *prm);
+}
+
+template <typename T, int W, bool SILU>
+cudaError_t shift_bwd_instance(SeqBwdParams* prm, const Plan* plan, cudaStream_t stream, int* nb_out) {
+  constexpr size_t smem =
+      (size_t)seq_bwd_stages<T>() * 2 * kRows * sh_row_bytes<T>() + 2 * seq_bwd_stages<T>() * sizeof(uint64_t);
+  static std::atomic<uint64_t> attr{0};
+  static std::atomic<int> occ{0};
+  int nb = 1;
+  cudaError_t e = prepare(bwd_shift_tma_kernel<T, W, SILU>, smem, attr, occ, &nb);
+  if (e != cudaSuccess) return e;
+  if (nb_out) *nb_out = nb;
+  if (prm == nullptr) return cudaSuccess;
+  return launch_pdl(bwd_shift_tma_kernel<T, W, SILU>, dim3((unsigned)plan->grid), dim3(kThreadsSeq), smem, stream,
+                    *prm);
+}
+
 struct SeqFwdOp {
   const FwdArgs& a;
   Plan* plan;
@@ -837,6 +1472,7 @@ struct SeqFwdOp {
   template <typename T, int W>
   cudaError_t operator()() {
     const bool silu = a.silu != 0;
+    const bool sh = fwd_shifted(sizeof(T), a);
     SeqFwdParams* prm = nullptr;
     SeqFwdParams storage;
     if (launch) {
@@ -844,13 +1480,20 @@ struct SeqFwdOp {
       storage.a.nseg = plan->nseg;
       storage.a.seg_len = plan->seg_len;
       storage.groups = plan->groups;
-      if (!make_seq_map<T>(&storage.map_x, a.x, a.L, a.D, a.B, a.xs_c, a.xs_b)) return cudaErrorInvalidValue;
+      const i64 ext = sh_extent(a.B, a.D, a.L, a.xs_c, a.xs_b);
+      storage.sg = sh_geom<T>(ext, a.L, plan->nseg, plan->seg_len);
+      const bool ok = sh ? make_sh_map<T>(&storage.map_x, a.x, ext, storage.sg)
+                         : make_seq_map<T>(&storage.map_x, a.x, a.L, a.D, a.B, a.xs_c, a.xs_b);
+      if (!ok) return cudaErrorInvalidValue;
       if (a.seq != nullptr && !make_ids_map(&storage.map_s, a.seq, a.L, a.B, a.ss_b)) return cudaErrorInvalidValue;
       prm = &storage;
     }
     int nb = 1;
     cudaError_t e;
-    if (a.seq != nullptr)
+    if (sh)
+      e = silu ? shift_fwd_instance<T, W, true>(prm, plan, stream, &nb)
+               : shift_fwd_instance<T, W, false>(prm, plan, stream, &nb);
+    else if (a.seq != nullptr)
       e = silu ? seq_fwd_instance<T, W, true, true>(prm, plan, stream, &nb)
                : seq_fwd_instance<T, W, true, false>(prm, plan, stream, &nb);
     else
@@ -874,6 +1517,7 @@ struct SeqBwdOp {
   template <typename T, int W>
   cudaError_t operator()() {
     const bool silu = a.silu != 0;
+    const bool sh = bwd_shifted(sizeof(T), a);
     SeqBwdParams* prm = nullptr;
     SeqBwdParams storage;
     if (launch) {
@@ -881,15 +1525,22 @@ struct SeqBwdOp {
       storage.a.nseg = plan->nseg;
       storage.a.seg_len = plan->seg_len;
       storage.groups = plan->groups;
-      if (!make_seq_map<T>(&storage.map_x, a.x, a.L, a.D, a.B, a.xs_c, a.xs_b) ||
-          !make_seq_map<T>(&storage.map_g, a.dout, a.L, a.D, a.B, a.gs_c, a.gs_b))
-        return cudaErrorInvalidValue;
+      const i64 ext = sh_extent(a.B, a.D, a.L, a.xs_c, a.xs_b);
+      storage.sg = sh_geom<T>(ext, a.L, plan->nseg, plan->seg_len);
+      const bool ok = sh ? (make_sh_map<T>(&storage.map_x, a.x, ext, storage.sg) &&
+                            make_sh_map<T>(&storage.map_g, a.dout, ext, storage.sg))
+                         : (make_seq_map<T>(&storage.map_x, a.x, a.L, a.D, a.B, a.xs_c, a.xs_b) &&
+                            make_seq_map<T>(&storage.map_g, a.dout, a.L, a.D, a.B, a.gs_c, a.gs_b));
+      if (!ok) return cudaErrorInvalidValue;
       if (a.seq != nullptr && !make_ids_map(&storage.map_s, a.seq, a.L, a.B, a.ss_b)) return cudaErrorInvalidValue;
       prm = &storage;
     }
     int nb = 1;
     cudaError_t e;
-    if (a.seq != nullptr)
+    if (sh)
+      e = silu ? shift_bwd_instance<T, W, true>(prm, plan, stream, &nb)
+               : shift_bwd_instance<T, W, false>(prm, plan, stream, &nb);
+    else if (a.seq != nullptr)
       e = silu ? seq_bwd_instance<T, W, true, true>(prm, plan, stream, &nb)
                : seq_bwd_instance<T, W, true, false>(prm, plan, stream, &nb);
     else
@@ -908,6 +1559,7 @@ struct SeqBwdOp {
 
 bool fwd_seq_tma_eligible(int dtype, const FwdArgs& a) {
   const int esz = esize(dtype);
+  if (encode_fn() != nullptr && fwd_shifted((size_t)esz, a)) return true;
   return (a.seq == nullptr || ids_ok(a.seq, a.ss_l, a.ss_b, a.B, a.L)) && seq_shape_ok(a.B, a.D, a.L) &&
          encode_fn() != nullptr &&
          seq_tensor_ok(a.x, a.xs_c, a.xs_l, a.xs_b, a.B, a.D, esz) &&
@@ -916,6 +1568,7 @@ bool fwd_seq_tma_eligible(int dtype, const FwdArgs& a) {
 
 bool bwd_seq_tma_eligible(int dtype, const BwdArgs& a) {
   const int esz = esize(dtype);
+  if (encode_fn() != nullptr && bwd_shifted((size_t)esz, a)) return true;
   return (a.seq == nullptr || ids_ok(a.seq, a.ss_l, a.ss_b, a.B, a.L)) && seq_shape_ok(a.B, a.D, a.L) &&
          encode_fn() != nullptr &&
          seq_tensor_ok(a.x, a.xs_c, a.xs_l, a.xs_b, a.B, a.D, esz) &&

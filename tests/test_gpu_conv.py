@@ -164,6 +164,53 @@ def test_seq_idx_vs_oracle(L, dtype, W, layout):
     _compare_oracle(x, w, b, seq, None, dout, None, W != 3, False, layout)
 
 
+@pytest.mark.parametrize("shape", [(2, 64, 9), (2, 64, 255), (2, 64, 257), (3, 24, 2047), (1, 16, 5001), (2, 65, 100),
+                                   (2, 65, 99)],
+                         ids=lambda s: "x".join(map(str, s)))
+@pytest.mark.parametrize("W", [2, 4])
+@pytest.mark.parametrize("dtype", ["fp32", "bf16", "fp16"])
+def test_contiguous_unaligned_rows_vs_oracle(shape, dtype, W):
+    """Contiguous rows whose pitch is not a multiple of 16 bytes (the
+    shifted-row TMA kernels: tiles on the tensor's 16-byte grid, row starts
+    inside a lane, row ends inside a tile, long rows split into segments),
+    with initial and final states.  The extents give view rows of 128 bytes
+    ((2, 64, 9)), 32 bytes ((1, 16, 5001) in 16-bit types) and 16 bytes
+    ((2, 65, 100) in 16-bit types); (2, 65, 99) in 16-bit types has an extent
+    that is not a whole number of 16-byte units and takes the register
+    kernels."""
+    dt = DTYPES[dtype]
+    B, D, L = shape
+    seed = 7 * L + W + D
+    x = seeded((B, D, L), dt, seed)
+    w = seeded((D, W), dt, seed + 1, "uniform")
+    b = seeded((D,), dt, seed + 2, "uniform")
+    init = seeded((B, D, W - 1), dt, seed + 3)
+    dout = seeded((B, D, L), dt, seed + 4)
+    dfinal = seeded((B, D, W - 1), dt, seed + 5)
+    _compare_oracle(x, w, b, None, init, dout, dfinal, True, True, "contig")
+
+
+@pytest.mark.parametrize("shape", [(3, 6400, 2101), (1, 5920, 4097)], ids=lambda s: "x".join(map(str, s)))
+@pytest.mark.parametrize("dtype", ["fp32", "bf16"])
+def test_contiguous_unaligned_long_segments_vs_oracle(shape, dtype):
+    """Unaligned contiguous rows with enough (batch, channel group) pairs
+    that segments span many tiles: the shared-memory ring wraps, the last
+    segment takes one tile more than its length when the row starts
+    mid-unit, and (second shape) a row splits into several multi-tile
+    segments."""
+    dt = DTYPES[dtype]
+    B, D, L = shape
+    W = 4
+    seed = 11 * L + D
+    x = seeded((B, D, L), dt, seed)
+    w = seeded((D, W), dt, seed + 1, "uniform")
+    b = seeded((D,), dt, seed + 2, "uniform")
+    init = seeded((B, D, W - 1), dt, seed + 3)
+    dout = seeded((B, D, L), dt, seed + 4)
+    dfinal = seeded((B, D, W - 1), dt, seed + 5)
+    _compare_oracle(x, w, b, None, init, dout, dfinal, True, True, "contig")
+
+
 @pytest.mark.parametrize("layout", ["contig", "chanlast"])
 @pytest.mark.parametrize("W", [2, 4])
 @pytest.mark.parametrize("dtype", ["fp32", "bf16"])
