@@ -59,6 +59,9 @@ namespace {
 #ifndef CC1D_SEQ_BWD_IDS_MIN_BLOCKS
 #define CC1D_SEQ_BWD_IDS_MIN_BLOCKS 3  // with seq_idx (174 registers uncapped: 2 blocks per SM)
 #endif
+#ifndef CC1D_SEQ_FWD_SH_MIN_BLOCKS
+#define CC1D_SEQ_FWD_SH_MIN_BLOCKS 5  // shifted rows: <= 80 registers, 5 blocks per SM (the smem limit)
+#endif
 #ifndef CC1D_SEQ_BWD_SH_MIN_BLOCKS
 #define CC1D_SEQ_BWD_SH_MIN_BLOCKS 3  // shifted rows (4 spills ~200 bytes at W = 4)
 #endif
@@ -807,7 +810,7 @@ __device__ __forceinline__ void shift_load_rows(unsigned char* dst, unsigned row
 }
 
 template <typename T, int W, bool SILU>
-__global__ void __launch_bounds__(kThreadsSeq, CC1D_SEQ_FWD_MIN_BLOCKS) fwd_shift_tma_kernel(const __grid_constant__ SeqFwdParams p) {
+__global__ void __launch_bounds__(kThreadsSeq, CC1D_SEQ_FWD_SH_MIN_BLOCKS) fwd_shift_tma_kernel(const __grid_constant__ SeqFwdParams p) {
   constexpr int H = W - 1;
   constexpr int E = unit_elems<T>();
   constexpr unsigned RB = sh_row_bytes<T>();
@@ -1058,13 +1061,6 @@ __global__ void __launch_bounds__(kThreadsSeq, W > 5 ? 1 : CC1D_SEQ_BWD_SH_MIN_B
 #pragma unroll
   for (int j = 0; j < H; ++j)
     carry[j] = xc_rows(xr, a.xs_c, a.xs_l, ir, a.is_c, a.is_l, H, t0 - off_a - H + j, t0 - off_b - H + j, va, vb);
-  // dpre just past each row's segment (0 past the row), for lane 31's last dx.
-  float2 rend[H];
-  {
-    const int ea = last_seg ? L : t0 + seg_len - off_a, eb = last_seg ? L : t0 + seg_len - off_b;
-#pragma unroll
-    for (int j = 0; j < H; ++j) rend[j] = dpre_rows<T, W, SILU>(xr, gr, ir, a, wp, bp, ea + j, eb + j, va, vb);
-  }
   // dinitial_states from dpre of positions 0 .. H-1, read directly.
   if (t0 == 0 && a.dinit != nullptr) {
     float2 dq[H];
@@ -1166,11 +1162,14 @@ __global__ void __launch_bounds__(kThreadsSeq, W > 5 ? 1 : CC1D_SEQ_BWD_SH_MIN_B
     qpb = qb;
   }
   if (ntiles > 0) {
+    // dpre just past each row's segment (0 past the row), for lane 31's last dx.
+    const int ea = last_seg ? L : t0 + seg_len - off_a, eb = last_seg ? L : t0 + seg_len - off_b;
     float2 rh[H];
 #pragma unroll
     for (int j = 0; j < H; ++j) {
       const float2 nxt = shfl_down2(dprev[j], 1);
-      rh[j] = lane == 31 ? rend[j] : nxt;
+      const float2 e = dpre_rows<T, W, SILU>(xr, gr, ir, a, wp, bp, ea + j, eb + j, va, vb);
+      rh[j] = lane == 31 ? e : nxt;
     }
     emit_dx_shift<T, W>(dprev, rh, wp, qpa, qpb, L, a, dxa, fa, va, vb);
   }
