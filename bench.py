@@ -504,6 +504,28 @@ def time_kernels(peak):
     del x, dout, out, dx
     torch.cuda.empty_cache()
 
+    # C2 shape with an odd length in the contiguous layout: row pitch
+    # 2047 * 2 bytes is not a multiple of 16 (shifted-row TMA kernels).
+    Bo, Do, Lo = 8, 5376, 2047
+    xo, douto = rn(Bo, Do, Lo), rn(Bo, Do, Lo)
+    wo, bo = ru(Do, W), ru(Do)
+    inito = rn(Bo, Do, W - 1)
+    outo, dxo, fso, dinito = torch.empty_like(xo), torch.empty_like(xo), torch.empty_like(inito), torch.empty_like(inito)
+    dwdbo = torch.empty(Do * (W + 1), dtype=torch.float32, device="cuda")
+    dwo, dbo = torch.empty(Do, W, dtype=DT, device="cuda"), torch.empty(Do, dtype=DT, device="cuda")
+    n = Bo * Do * Lo
+    ms = _kernel_ms(lambda i: _ops.fwd(xo, wo, bo, None, inito, outo, True, fso), 40, 1)
+    nb = 4 * n + 2 * inito.numel() * 2 + Do * (W + 1) * 2
+    res["fwd_c2_odd_len_contiguous"] = dict(ms=ms, gbs=nb / ms / 1e6, frac=nb / ms / 1e6 / peak,
+                                            tokens_per_s=Bo * Lo / (ms / 1e3), algorithmic_bytes=nb,
+                                            note="(8, 5376, 2047) bf16 contiguous: row pitch not 16-byte aligned")
+    ms = _kernel_ms(lambda i: _ops.bwd(xo, wo, bo, douto, None, inito, None, dxo, dwdbo, dinito, dwo, dbo, True), 40, 1)
+    nb = 6 * n + 2 * inito.numel() * 2 + Do * (W + 1) * (2 + 2 + 4)
+    res["bwd_c2_odd_len_contiguous"] = dict(ms=ms, gbs=nb / ms / 1e6, frac=nb / ms / 1e6 / peak,
+                                            tokens_per_s=Bo * Lo / (ms / 1e3), algorithmic_bytes=nb)
+    del xo, douto, outo, dxo
+    torch.cuda.empty_cache()
+
     # C5: large contiguous (64, 8192, 8192) bf16, width 4, SiLU, states on.
     B5, D5, L5 = 64, 8192, 8192
     x = rn(B5, D5, L5)
