@@ -190,6 +190,23 @@ def test_contiguous_unaligned_rows_vs_oracle(shape, dtype, W):
     _compare_oracle(x, w, b, None, init, dout, dfinal, True, True, "contig")
 
 
+@pytest.mark.parametrize("dtype,W", [("bf16", 5), ("bf16", 7), ("bf16", 9), ("fp16", 9), ("fp32", 5)])
+def test_contiguous_unaligned_wide_widths_vs_oracle(dtype, W):
+    """Wide kernels on rows whose pitch is not a multiple of 16 bytes: the
+    halo reaches up to 8 positions back, across the lane whose first tile
+    element sits before the row start."""
+    dt = DTYPES[dtype]
+    B, D, L = 2, 48, 2047
+    seed = 13 * W + L
+    x = seeded((B, D, L), dt, seed)
+    w = seeded((D, W), dt, seed + 1, "uniform")
+    b = seeded((D,), dt, seed + 2, "uniform")
+    init = seeded((B, D, W - 1), dt, seed + 3)
+    dout = seeded((B, D, L), dt, seed + 4)
+    dfinal = seeded((B, D, W - 1), dt, seed + 5)
+    _compare_oracle(x, w, b, None, init, dout, dfinal, True, True, "contig")
+
+
 @pytest.mark.parametrize("shape", [(3, 6400, 2101), (1, 5920, 4097)], ids=lambda s: "x".join(map(str, s)))
 @pytest.mark.parametrize("dtype", ["fp32", "bf16"])
 def test_contiguous_unaligned_long_segments_vs_oracle(shape, dtype):
