@@ -172,6 +172,30 @@ def barrier_sync(world):
     torch.cuda.synchronize()
 
 
+def device_rendezvous(world):
+    """Align the ranks ON THE DEVICE right before a start event: a one-word
+    all-reduce on the current stream completes at nearly the same moment on
+    every GPU, whereas host processes leave a barrier up to ~100 us apart.
+    Without it, the first cross-rank exchange of a short timed region is
+    charged with that host skew on the ranks that started first."""
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.all_reduce(torch.zeros(1, device="cuda"))
+
+
+def gather_floats(vals, world):
+    """Every rank's list of floats (same length on all ranks), rank order."""
+    if world == 1:
+        return [list(vals)]
+    import torch.distributed as dist
+
+    t = torch.tensor(vals, dtype=torch.float64, device="cuda")
+    parts = [torch.empty_like(t) for _ in range(world)]
+    dist.all_gather(parts, t)
+    return [p.tolist() for p in parts]
+
+
 # --------------------------------------------------------------------------
 # our arm
 # --------------------------------------------------------------------------
@@ -257,6 +281,7 @@ def time_c2(args, world, rank, reducer):
             g_step.replay()
         barrier_sync(world)
         clk.mark()
+        device_rendezvous(world)
         start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         start.record()
         for _ in range(K):
@@ -264,15 +289,202 @@ def time_c2(args, world, rank, reducer):
         stop.record()
         torch.cuda.synchronize()
         clk.unmark()
+        barrier_sync(world)
     total_ms = start.elapsed_time(stop)
     # Per-op kernel times: graphs of the op alone, replayed back to back.
     reps = max(20, min(200, K // 10))
-    fwd_ms = graph_ms(graph_of(fwd, 10), reps, 10)
-    bwd_ms = graph_ms(graph_of(bwd, 10), reps, 10)
-    del g_step
+    g_fwd, g_bwd = graph_of(fwd, 10), graph_of(bwd, 10)
     barrier_sync(world)
+    device_rendezvous(world)
+    fwd_ms = graph_ms(g_fwd, reps, 10)
+    barrier_sync(world)
+    device_rendezvous(world)
+    bwd_ms = graph_ms(g_bwd, reps, 10)
+    del g_step, g_fwd, g_bwd
+    barrier_sync(world)
+    extra = {}
+    if world > 1:
+        # Each rank's step with a local reduction only (no exchange, no
+        # waiting for peers): the spread of these is the GPUs' own speed
+        # difference, which a synchronous data-parallel step cannot hide.
+        def local_step(_=0):
+            fwd()
+            _ops.bwd(x, w, b, dout, None, init, None, dx, dwdb, dinit, dw, db, True)
+
+        local_ms = graph_ms(graph_of(local_step, 10), reps, 10)
+        per_rank = gather_floats([total_ms / K, bwd_ms, local_ms], world)
+        extra["per_rank"] = {
+            "step_ms": [r[0] for r in per_rank],
+            "bwd_with_exchange_ms": [r[1] for r in per_rank],
+            "step_local_reduction_ms": [r[2] for r in per_rank],
+            "note": "step_local_reduction_ms: the same fwd+bwd with the dweight/dbias reduction kept on the "
+                    "rank (no exchange); its max over ranks bounds a synchronous step from below",
+        }
+        extra["parity"] = peer_parity(x, w, b, dout, init, dwdb, dw, db, world)
+    extra["parity_c2"] = c2_parity(x, w, b, init, dout, out, fs, dx, dinit, dw, db) if rank == 0 else None
     total_ms = max_over_ranks(total_ms, world)
-    return dict(ms_per_step=total_ms / K, fwd_ms=fwd_ms, bwd_ms=bwd_ms, clocks=clk.summary())
+    return dict(ms_per_step=total_ms / K, fwd_ms=fwd_ms, bwd_ms=bwd_ms, clocks=clk.summary(), **extra)
+
+
+def peer_parity(x, w, b, dout, init, dwdb_fused, dw_fused, db_fused, world):
+    """After the timed region: every rank recomputes its shard's backward
+    with the plain single-GPU reduction, the fp32 [dweight | dbias] buffers
+    are gathered over NCCL and summed in rank order, and the result must be
+    BITWISE equal to what the fused peer-exchange kernel left on this rank
+    (fp32 and the bf16 copies).  Returns the verdict of all ranks."""
+    import torch.distributed as dist
+
+    from causal_conv1d_b200 import _ops
+
+    torch.cuda.synchronize()
+    dwdb = torch.empty_like(dwdb_fused)
+    _ops.bwd(x, w, b, dout, None, init, None, torch.empty_like(x), dwdb, torch.empty_like(init), None, None, True)
+    parts = [torch.empty_like(dwdb) for _ in range(world)]
+    dist.all_gather(parts, dwdb)
+    total = torch.zeros_like(dwdb)
+    for p in parts:
+        total = total + p
+    ok = (torch.equal(dwdb_fused, total) and torch.equal(dw_fused, total[: D * W].view(D, W).to(DT))
+          and torch.equal(db_fused, total[D * W:].to(DT)))
+    flags = torch.tensor([1 if ok else 0], dtype=torch.int32, device="cuda")
+    every = [torch.empty_like(flags) for _ in range(world)]
+    dist.all_gather(every, flags)
+    good = [int(f.item()) for f in every]
+    return {"peer_dwdb_bitwise": all(good), "ranks_checked": world, "ranks_ok": sum(good),
+            "how": "fused peer-exchange dweight|dbias (fp32 and bf16) == rank-order sum of per-rank "
+                   "single-GPU results gathered over NCCL, on every rank"}
+
+
+def c2_parity(x, w, b, init, dout, out, fs, dx, dinit, dw, db):
+    """Whole-tensor check of the timed C2 step's results against an fp32
+    evaluation of the pure-PyTorch reference (causal_conv1d_ref + autograd)
+    on the GPU: bf16 outputs within rtol = atol = 1e-2, weight gradients
+    within 1e-2 x max|ref|, final_states bit-exact.  The last replay of the
+    step left its results in these buffers; the backward is rerun here with
+    the local reduction so that dw/db are this rank's own (with N GPUs the
+    timed buffers hold the cross-rank sums)."""
+    from causal_conv1d_b200 import _ops, causal_conv1d_ref
+
+    dwdb = torch.empty(D * (W + 1), dtype=torch.float32, device="cuda")
+    dw1, db1 = torch.empty_like(dw), torch.empty_like(db)
+    _ops.bwd(x, w, b, dout, None, init, None, dx, dwdb, dinit, dw1, db1, True)
+    xf = x.detach().float().requires_grad_()
+    wf = w.detach().float().requires_grad_()
+    bf = b.detach().float().requires_grad_()
+    inf = init.detach().float().requires_grad_()
+    ro, rfs = causal_conv1d_ref(xf, wf, bf, initial_states=inf, return_final_states=True, activation="silu")
+    ro.backward(dout.float())
+
+    def worst(a, e, atol, rtol=1e-2):
+        a, e = a.float(), e.float()
+        bad = ~((a - e).abs() <= atol + rtol * e.abs())
+        return int(bad.sum()), float((a - e).abs().max())
+
+    norm = max(wf.grad.abs().max().item(), bf.grad.abs().max().item())
+    checks = {"out": worst(out, ro.detach(), 1e-2), "dx": worst(dx, xf.grad, 1e-2),
+              "dinit": worst(dinit, inf.grad, 1e-2), "dweight": worst(dw1, wf.grad, 1e-2 * max(1.0, norm)),
+              "dbias": worst(db1, bf.grad, 1e-2 * max(1.0, norm))}
+    fs_exact = torch.equal(fs, rfs.detach().to(DT))
+    return {"whole_tensor_ok": all(n == 0 for n, _ in checks.values()) and fs_exact,
+            "final_states_bitwise": fs_exact,
+            "max_abs_err": {k: v for k, (_, v) in checks.items()},
+            "out_of_tolerance": {k: n for k, (n, _) in checks.items()},
+            "how": "C2 step outputs vs causal_conv1d_ref in fp32 on the GPU (bf16 inputs upcast): rtol=atol=1e-2, "
+                   "weight grads atol 1e-2*max|ref|; every element of every tensor"}
+
+
+C5_B, C5_D, C5_L = 64, 8192, 8192
+
+
+def time_c5_sweep(world, rank, local, peak):
+    """the large (64, 8192, 8192) bf16 problem,
+    forward + backward with initial and final states, widths 2/3/4, SiLU on
+    and off, split over the `world` GPUs two ways (strong scaling: the job is
+    the whole problem at every N):
+
+      batch -- rank r owns batch rows shard_range(64, r, N) and the full
+               weights; the backward's dweight/dbias sum over the ranks runs
+               inside its reduction kernel (NVLink peer exchange);
+      dim   -- rank r owns channels shard_range(8192, r, N) with the matching
+               weight / bias / state slices; no communication at all.
+
+    Each op is timed alone (a CUDA graph of 4 launches replayed, device-side
+    rendezvous before the start event), max over ranks.  At N = 1 both splits
+    are the same single-GPU problem, reported once as "single"."""
+    from causal_conv1d_b200 import _ops
+    from causal_conv1d_b200.parallel import PeerReducer, shard_range
+
+    g = torch.Generator(device="cuda").manual_seed(50 + rank)
+
+    def rn(*sh):
+        return torch.randn(*sh, generator=g, device="cuda", dtype=torch.float32).to(DT)
+
+    def ru(*sh):
+        return (torch.rand(*sh, generator=g, device="cuda", dtype=torch.float32) - 0.5).to(DT)
+
+    def op_ms(fn):
+        fn()
+        torch.cuda.synchronize()
+        gr = graph_of(lambda i: fn(), 4)
+        barrier_sync(world)
+        device_rendezvous(world)
+        ms = graph_ms(gr, 2, 4)
+        del gr
+        barrier_sync(world)
+        return max_over_ranks(ms, world)
+
+    out_tab = {}
+    for sh in (("batch", "dim") if world > 1 else ("single",)):
+        if sh == "batch":
+            b0, b1 = shard_range(C5_B, rank, world)
+            Bl, Dl = b1 - b0, C5_D
+        elif sh == "dim":
+            d0, d1 = shard_range(C5_D, rank, world)
+            Bl, Dl = C5_B, d1 - d0
+        else:
+            Bl, Dl = C5_B, C5_D
+        x, dout = rn(Bl, Dl, C5_L), rn(Bl, Dl, C5_L)
+        out, dx = torch.empty_like(x), torch.empty_like(x)
+        n = Bl * Dl * C5_L
+        rows = []
+        for width in (2, 3, 4):
+            w, b = ru(Dl, width), ru(Dl)
+            init = rn(Bl, Dl, width - 1)
+            fs, dinit = torch.empty_like(init), torch.empty_like(init)
+            dwdb = torch.empty(Dl * (width + 1), dtype=torch.float32, device="cuda")
+            dw = torch.empty(Dl, width, dtype=DT, device="cuda")
+            db = torch.empty(Dl, dtype=DT, device="cuda")
+            reducer = PeerReducer(Dl, width, torch.device("cuda", local)) if sh == "batch" else None
+            for silu in (True, False):
+                def fwd(silu=silu):
+                    _ops.fwd(x, w, b, None, init, out, silu, fs)
+
+                def bwd(silu=silu):
+                    if reducer is not None:
+                        _ops.bwd_peer(x, w, b, dout, init, None, dx, dwdb, dinit, dw, db, silu, *reducer.args())
+                    else:
+                        _ops.bwd(x, w, b, dout, None, init, None, dx, dwdb, dinit, dw, db, silu)
+
+                fms, bms = op_ms(fwd), op_ms(bwd)
+                fb = 4 * n + 2 * init.numel() * 2 + Dl * (width + 1) * 2
+                bb = 6 * n + 2 * init.numel() * 2 + Dl * (width + 1) * (2 + 2 + 4)
+                rows.append({"width": width, "silu": silu, "fwd_ms": fms, "bwd_ms": bms,
+                             "tokens_per_s": C5_B * C5_L / ((fms + bms) / 1e3),
+                             "fwd_frac": fb / fms / 1e6 / peak, "bwd_frac": bb / bms / 1e6 / peak,
+                             "fwd_bytes_per_gpu": fb, "bwd_bytes_per_gpu": bb})
+            if reducer is not None:
+                if rank == 0:
+                    reducer.check()
+                reducer.close()
+            del w, b, init, fs, dinit, dwdb, dw, db
+        del x, dout, out, dx
+        torch.cuda.empty_cache()
+        out_tab[sh] = {"per_gpu_shape_rank0": [Bl, Dl, C5_L], "rows": rows}
+    return {"workload": "BASELINE configs[4]: x (64, 8192, 8192) bf16 contiguous, fwd+bwd, initial + final states, "
+                        "width 2/3/4, SiLU on/off; whole problem split over the GPUs (strong scaling)",
+            "n_gpus": world, "timing": "each op alone, CUDA graph of 4 launches x 2 replays, max over ranks; "
+                                       "fractions per GPU against the measured HBM copy peak",
+            "shardings": out_tab}
 
 
 def gpu_local_cpus(dev_index):
@@ -391,6 +603,47 @@ def _kernel_ms(fn, iters, sets):
     return graph_ms(g, max(1, iters // n), n)
 
 
+def decode_sweep(w, b, rn, peak):
+    from causal_conv1d_b200 import _ops
+
+    Du = w.shape[0]
+    sets = 8
+    out = {}
+    for mode in ("c3a_indexed", "c3b_circular"):
+        pts = []
+        for Bs in (1, 256, 384, 512, 768, 1024):
+            xs = [rn(Bs, Du, 1) for _ in range(sets)]
+            outs = [torch.empty_like(xs[0]) for _ in range(sets)]
+            if mode == "c3a_indexed":
+                pools = [rn(2 * Bs, Du, W - 1) for _ in range(sets)]
+                idx = [torch.randperm(2 * Bs, device="cuda")[:Bs].to(torch.int32) for _ in range(sets)]
+                ms = _kernel_ms(lambda i: _ops.update(xs[i], pools[i], w, b, None, idx[i], outs[i], True), 800, sets)
+                row = Du * (2 + 2 + 6 + 6)
+                del pools, idx
+            else:
+                sts = [rn(Bs, Du, 8) for _ in range(sets)]
+                cache = [torch.randint(0, 1024, (Bs,), device="cuda", dtype=torch.int32) for _ in range(sets)]
+                ms = _kernel_ms(lambda i: _ops.update(xs[i], sts[i], w, b, cache[i], None, outs[i], True), 800, sets)
+                row = Du * (2 + 2 + 6 + 2)
+                del sts, cache
+            pts.append((Bs, ms * 1e3, Bs * row))
+            del xs, outs
+        fit = [p for p in pts if p[0] >= 256]
+        n = len(fit)
+        mx = sum(p[0] for p in fit) / n
+        my = sum(p[1] for p in fit) / n
+        slope = sum((p[0] - mx) * (p[1] - my) for p in fit) / sum((p[0] - mx) ** 2 for p in fit)
+        t0 = my - slope * mx
+        row_bytes = pts[0][2] / pts[0][0]
+        out[mode] = {"batch_us": {str(p[0]): p[1] for p in pts}, "fit_batches": [p[0] for p in fit],
+                     "fit_floor_us": t0, "fit_us_per_row": slope,
+                     "fit_transfer_gbs": row_bytes / (slope * 1e-6) / 1e9,
+                     "fit_transfer_frac": row_bytes / (slope * 1e-6) / 1e9 / peak,
+                     "row_bytes_algorithmic": row_bytes}
+    torch.cuda.empty_cache()
+    return out
+
+
 def time_kernels(peak):
     """Secondary kernels of the metric, each timed alone."""
     from causal_conv1d_b200 import _ops
@@ -426,6 +679,15 @@ def time_kernels(peak):
                                       tokens_per_s=Bu / (ms / 1e3), algorithmic_bytes=nbytes)
     del states, xs, outs
     torch.cuda.empty_cache()
+
+    # Fixed cost of a decode step: the same two kernels over a range of batch
+    # sizes in the same harness.  A least-squares line t(B) = t0 + B * s over
+    # the batches whose 8 rotating buffer sets exceed L2 (B >= 256) splits
+    # the C3 time into a per-launch floor t0 (launch, the dependent index ->
+    # state round trips, the last wave's drain) and a transfer part whose
+    # bandwidth is row_bytes / s.  B = 1 is reported alone (its data sits in
+    # L2: pure fixed cost).
+    res["decode_batch_sweep"] = decode_sweep(w, b, rn, peak)
 
     # Next rows of the path: a 4-token decode burst (speculative decoding) on
     # the C3a pool, and the C3a step with a channel-last conv_state pool
@@ -526,29 +788,6 @@ def time_kernels(peak):
     del xo, douto, outo, dxo
     torch.cuda.empty_cache()
 
-    # C5: large contiguous (64, 8192, 8192) bf16, width 4, SiLU, states on.
-    B5, D5, L5 = 64, 8192, 8192
-    x = rn(B5, D5, L5)
-    out = torch.empty_like(x)
-    w5, b5 = ru(D5, W), ru(D5)
-    init = rn(B5, D5, W - 1)
-    fs = torch.empty_like(init)
-    n = B5 * D5 * L5
-    ms = _kernel_ms(lambda i: _ops.fwd(x, w5, b5, None, init, out, True, fs), 5, 1)
-    nb = 4 * n + 2 * init.numel() * 2 + D5 * (W + 1) * 2
-    res["fwd_c5_large"] = dict(ms=ms, gbs=nb / ms / 1e6, frac=nb / ms / 1e6 / peak,
-                               tokens_per_s=B5 * L5 / (ms / 1e3), algorithmic_bytes=nb)
-    dout = out  # reuse the buffer as grad_out (values irrelevant for timing)
-    dx = torch.empty_like(x)
-    dwdb = torch.empty(D5 * (W + 1), dtype=torch.float32, device="cuda")
-    dw, db, dinit = torch.empty(D5, W, dtype=DT, device="cuda"), torch.empty(D5, dtype=DT, device="cuda"), \
-        torch.empty_like(init)
-    ms = _kernel_ms(lambda i: _ops.bwd(x, w5, b5, dout, None, init, None, dx, dwdb, dinit, dw, db, True), 5, 1)
-    nb = 6 * n + 2 * init.numel() * 2 + D5 * (W + 1) * (2 + 2 + 4)
-    res["bwd_c5_large"] = dict(ms=ms, gbs=nb / ms / 1e6, frac=nb / ms / 1e6 / peak,
-                               tokens_per_s=B5 * L5 / (ms / 1e3), algorithmic_bytes=nb)
-    del x, out, dx
-    torch.cuda.empty_cache()
     return res
 
 
@@ -632,17 +871,22 @@ def run_reference(args):
         t0 = time.perf_counter_ns()
         cpu_sample_step(state)
         times.append((time.perf_counter_ns() - t0) / 1e9)
-    ms = 1e3 * sum(times) / len(times)
+    # The reference's own CPU timing method: the minimum over samples of
+    # perf_counter_ns around each call (scripts/plot_bench.py:225-243).
+    ms = 1e3 * min(times)
     value = L / (ms / 1e3)
     line = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+        "ms_per_step_unit": f"one step = one C2 batch row (1, {D}, {L}) fwd+bwd on the host cores, the minimum "
+                            f"over the {len(times)} timed steps; the C2 batch has {B} such rows",
+        "ms_per_step_mean": 1e3 * sum(times) / len(times),
         "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
         "config": c2_config(args.gpus),
         "cpu_baseline": {"value": value, "unit": UNIT, "cores": cores, "kind": "port",
                          "sample": f"batch row 0 (1, {D}, {L}) of C2 per step (tokens/s of that row, all host "
-                                   f"threads); reference CPU algorithm (oracle/cc1d_oracle.c, restating "
-                                   f"fwd_cpu/bwd_full_cpu kernel.mojo)"},
+                                   f"threads, min over steps); reference CPU algorithm (oracle/cc1d_oracle.c, "
+                                   f"restating fwd_cpu/bwd_full_cpu kernel.mojo)"},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -747,6 +991,7 @@ def main():
     ap.add_argument("--skip-kernels", action="store_true", help="skip the secondary kernel table")
     ap.add_argument("--skip-e2e", action="store_true")
     ap.add_argument("--skip-cpu", action="store_true")
+    ap.add_argument("--skip-c5", action="store_true", help="skip the C5 sweep (BASELINE configs[4])")
     ap.add_argument("--only", default=None,
                     help="launch one op alone (fwd_c2, bwd_c2, update_c3a, update_c3b, update_burst4, "
                          "update_c3a_chanlast, fwd_c4, bwd_c4, fwd_c5, bwd_c5) --reps times, for profilers; "
@@ -774,6 +1019,7 @@ def main():
         reducer = PeerReducer(D, W, torch.device("cuda", local))
     r = time_c2(args, world, rank, reducer)
     e2e = None if args.skip_e2e else time_e2e(args, world, rank, reducer)
+    c5 = None if args.skip_c5 else time_c5_sweep(world, rank, local, peak)
     kernels = None
     if rank == 0 and not args.skip_kernels:
         kernels = time_kernels(peak)
@@ -796,6 +1042,13 @@ def main():
         }
         if kernels:
             ktab.update(kernels)
+        if c5 is not None and world == 1:
+            # The sweep's width-4 SiLU row on one GPU is the C5 kernel line.
+            row = next(x for x in c5["shardings"]["single"]["rows"] if x["width"] == W and x["silu"])
+            for op in ("fwd", "bwd"):
+                ms, nb = row[f"{op}_ms"], row[f"{op}_bytes_per_gpu"]
+                ktab[f"{op}_c5_large"] = dict(ms=ms, gbs=nb / ms / 1e6, frac=nb / ms / 1e6 / peak,
+                                              tokens_per_s=C5_B * C5_L / (ms / 1e3), algorithmic_bytes=nb)
         line = {
             "metric": METRIC,
             "value": world * B * L / (r["ms_per_step"] / 1e3),
@@ -820,7 +1073,13 @@ def main():
             "kernels": ktab,
             "gpu_launches": 3 * args.steps,
             "clocks": r["clocks"],
+            "parity": {k: v for k, v in (("peer_reduction", r.get("parity")), ("c2_step", r.get("parity_c2")))
+                       if v is not None},
         }
+        if "per_rank" in r:
+            line["per_rank"] = r["per_rank"]
+        if c5 is not None:
+            line["c5_sweep"] = c5
         if e2e is not None:
             line["e2e"] = e2e
         if cpu is not None:

@@ -98,7 +98,7 @@ class VarlenParams(ctypes.Structure):
 
 class PeerReduceParams(ctypes.Structure):
     _fields_ = [("rank", c_i32), ("world", c_i32), ("exchange", c_ptr), ("epochs", c_ptr),
-                ("max_polls", ctypes.c_uint32), ("reserved", ctypes.c_uint32)]
+                ("max_polls", ctypes.c_uint32), ("reserved", ctypes.c_uint32), ("status", c_ptr)]
 
 
 # Every symbol include/cc1d.h declares, with its ctypes signature.
@@ -158,10 +158,28 @@ def check(status: int, what: str) -> None:
         raise Cc1dError(status, f"{what} failed (status {status}): {msg}")
 
 
-def device_wait_timeouts() -> int:
-    """Bounded in-kernel waits that gave up since the last call (and reset
-    the count); synchronises the current device."""
+def device_wait_timeouts(device=None) -> int:
+    """Bounded in-kernel waits that gave up on `device` (default: the current
+    CUDA device) since the last call for that device, and reset its count;
+    synchronises that device.  The counts are per device: a process driving
+    several GPUs asks each one (``device_wait_timeouts(d)`` for every d)."""
+    import torch
+
     lib = load()
     n = ctypes.c_uint(0)
-    check(lib.cc1d_device_status(ctypes.byref(n)), "cc1d_device_status")
+    prev = torch.cuda.current_device()
+    if device is None:
+        dev = prev
+    elif isinstance(device, int):
+        dev = device
+    else:
+        dev = torch.device(device).index
+        dev = prev if dev is None else dev
+    try:
+        if dev != prev:
+            torch.cuda.set_device(dev)
+        check(lib.cc1d_device_status(ctypes.byref(n)), "cc1d_device_status")
+    finally:
+        if dev != prev:
+            torch.cuda.set_device(prev)
     return int(n.value)

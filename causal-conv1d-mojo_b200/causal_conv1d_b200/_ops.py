@@ -222,11 +222,16 @@ def _bwd_peer_impl(
     epochs: torch.Tensor,
     rank: int,
     world: int,
-    max_polls: int = 0,
+    max_polls: int,
+    status: torch.Tensor | None,
 ) -> None:
     """Backward of a batch shard with dweight/dbias summed over `world` ranks
     in the same kernel (cc1d_bwd_peer_reduce).  exchange_ptrs: int64 device
-    tensor of the ranks' peer-mapped exchange buffer addresses."""
+    tensor of the ranks' peer-mapped exchange buffer addresses.  status:
+    optional int32 device word, incremented by every wait for a peer that
+    gave up (the outputs it could not reduce are written as NaN).
+    max_polls (0 = the library default) and status are passed explicitly:
+    a mutated argument of a custom op must be present in every call."""
     _require_cuda(x, "causal_conv1d_fn backward (peer reduce)")
     lib = _lib.load()
     p = _bwd_params(x, weight, bias, dout, None, initial_states, dfinal_states, dx, dwdb_acc, dinitial_states,
@@ -235,6 +240,7 @@ def _bwd_peer_impl(
     q.rank, q.world = rank, world
     q.exchange, q.epochs = exchange_ptrs.data_ptr(), epochs.data_ptr()
     q.max_polls = max_polls
+    q.status = _ptr(status)
     with _on_device(x.device):
         nbytes = bwd_workspace_bytes(p)
         ws = None
@@ -248,13 +254,14 @@ def _bwd_peer_impl(
 
 
 def _bwd_peer_fake(x, weight, bias, dout, initial_states, dfinal_states, dx, dwdb_acc, dinitial_states,
-                   dweight_out, dbias_out, apply_silu, exchange_ptrs, epochs, rank, world, max_polls=0) -> None:
+                   dweight_out, dbias_out, apply_silu, exchange_ptrs, epochs, rank, world, max_polls,
+                   status) -> None:
     return None
 
 
 bwd_peer = torch.library.custom_op(
     "causal_conv1d_b200::bwd_peer",
-    mutates_args=("dx", "dwdb_acc", "dinitial_states", "dweight_out", "dbias_out", "epochs"),
+    mutates_args=("dx", "dwdb_acc", "dinitial_states", "dweight_out", "dbias_out", "epochs", "status"),
 )(_bwd_peer_impl)
 bwd_peer.register_fake(_bwd_peer_fake)
 

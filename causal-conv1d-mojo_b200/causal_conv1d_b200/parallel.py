@@ -15,10 +15,14 @@ with no data exchange:
 Two implementations of that all-reduce:
 
 * ``PeerReducer`` (GPUs on one node): the backward's final reduction kernel
-  also performs the cross-GPU sum, reading the peers' partial sums over
-  NVLink from IPC-mapped buffers (cc1d_bwd_peer_reduce).  One launch replaces
-  finalize -> all-reduce -> dtype casts, and every rank gets bitwise
-  identical gradients, summed in rank order.
+  also performs the cross-GPU sum (cc1d_bwd_peer_reduce).  Each rank PUSHES
+  its local sums over NVLink into every peer's IPC-mapped exchange buffer
+  with plain peer stores, then reads only its OWN buffer (local memory) and
+  adds the ranks' values in rank order.  One launch replaces finalize ->
+  all-reduce -> dtype casts, and every rank gets bitwise identical
+  gradients.  A rank that is late beyond the bounded wait (or gone) makes
+  the others write NaN gradients and count the event in the reducer's status
+  word, which ``PeerReducer.check()`` turns into an exception.
 * ``allreduce_weight_grads``: one ``torch.distributed`` all-reduce of the
   fp32 buffer (NCCL on GPUs; the host logic is exercised with gloo on CPU).
 
@@ -67,6 +71,15 @@ def allreduce_weight_grads(dwdb: torch.Tensor, group=None) -> torch.Tensor:
     return dwdb
 
 
+def _cuda_device(device) -> torch.device:
+    dev = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
+    if dev.type != "cuda":
+        raise ValueError("PeerReducer needs a CUDA device")
+    if dev.index is None:
+        dev = torch.device("cuda", torch.cuda.current_device())
+    return dev
+
+
 def _rt_check(res, what: str):
     err = res[0] if isinstance(res, tuple) else res
     if int(err) != 0:
@@ -88,9 +101,17 @@ class PeerReducer:
     same sequence of backward calls with the same dim/width.  The per-block
     call counters live on the device, so those calls may be captured in a
     CUDA graph and replayed.
+
+    Failure detection: every wait for a peer is bounded (`max_polls` polls,
+    0 = the library default of about a second or more).  A wait that gives
+    up writes NaN into the gradients it could not reduce and adds 1 to this
+    reducer's device status word; ``check()`` -- call it at a point where the
+    host synchronises anyway, e.g. right before the optimizer step -- raises
+    if any call since the previous check gave up.
     """
 
-    def __init__(self, dim: int, width: int, device: torch.device | str | int | None = None, group=None):
+    def __init__(self, dim: int, width: int, device: torch.device | str | int | None = None, group=None,
+                 max_polls: int = 0):
         from cuda.bindings import runtime as rt
 
         if not (dist.is_available() and dist.is_initialized()):
@@ -101,12 +122,10 @@ class PeerReducer:
         self.world = dist.get_world_size(group)
         if self.world > 32:
             raise ValueError("PeerReducer supports at most 32 ranks")
-        dev = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
-        if dev.type != "cuda":
-            raise ValueError("PeerReducer needs a CUDA device")
-        if dev.index is None:
-            dev = torch.device("cuda", torch.cuda.current_device())
+        dev = _cuda_device(device)
         self.device, self.dim, self.width = dev, dim, width
+        self.max_polls = int(max_polls)
+        self._collective = True
         lib = _lib.load()
         self.nblocks = int(lib.cc1d_peer_blocks(dim, width))
         nbytes = max(int(lib.cc1d_peer_exchange_bytes(dim, width, self.world)), 16)
@@ -137,18 +156,70 @@ class PeerReducer:
             ptrs[r] = int(mp)
         self.exchange_ptrs = torch.tensor(ptrs, dtype=torch.int64, device=dev)
         self.epochs = torch.zeros(max(self.nblocks, 1), dtype=torch.int32, device=dev)
+        self.status = torch.zeros(1, dtype=torch.int32, device=dev)
         torch.cuda.synchronize(dev)
         dist.barrier(group=group)
 
-    def args(self) -> tuple[torch.Tensor, torch.Tensor, int, int]:
-        """(exchange_ptrs, epochs, rank, world) for ``_ops.bwd_peer``."""
+    @classmethod
+    def from_exchange(cls, exchange_ptrs: torch.Tensor, rank: int, dim: int, width: int, max_polls: int = 0):
+        """A reducer over exchange buffers the caller mapped itself (its own
+        IPC layer, or one process owning several buffers): `exchange_ptrs`
+        is an int64 device tensor of the `world` buffer addresses, each
+        cc1d_peer_exchange_bytes(dim, width, world) bytes and zeroed.  No
+        collective is made and ``close()`` frees nothing; the caller keeps
+        the buffers alive while the reducer is used."""
+        if exchange_ptrs.dtype != torch.int64 or exchange_ptrs.dim() != 1 or not exchange_ptrs.is_cuda:
+            raise ValueError("exchange_ptrs must be a 1-D int64 CUDA tensor")
+        world = exchange_ptrs.numel()
+        if not 1 <= world <= 32 or not 0 <= rank < world:
+            raise ValueError(f"bad rank {rank} for world size {world} (at most 32)")
+        self = cls.__new__(cls)
+        self._rt = None
+        self.group = None
+        self.rank, self.world = int(rank), int(world)
+        self.device = exchange_ptrs.device
+        self.dim, self.width = dim, width
+        self.max_polls = int(max_polls)
+        self._collective = False
+        self.nblocks = int(_lib.load().cc1d_peer_blocks(dim, width))
+        self._own = 0
+        self._mapped = []
+        self.exchange_ptrs = exchange_ptrs
+        self.epochs = torch.zeros(max(self.nblocks, 1), dtype=torch.int32, device=self.device)
+        self.status = torch.zeros(1, dtype=torch.int32, device=self.device)
+        return self
+
+    def args(self) -> tuple[torch.Tensor, torch.Tensor, int, int, int, torch.Tensor]:
+        """(exchange_ptrs, epochs, rank, world, max_polls, status) for
+        ``_ops.bwd_peer``."""
         if self._own is None:
             raise RuntimeError("PeerReducer is closed")
-        return self.exchange_ptrs, self.epochs, self.rank, self.world
+        return self.exchange_ptrs, self.epochs, self.rank, self.world, self.max_polls, self.status
+
+    def failed_waits(self) -> int:
+        """Waits for a peer that gave up since the last ``check()`` (reads
+        the device word: synchronises with this device's queued work)."""
+        return int(self.status.item())
+
+    def check(self) -> None:
+        """Raise if a backward call through this reducer gave up waiting for
+        a peer since the previous check (its weight/bias gradients then hold
+        NaN where the cross-rank sum could not be formed).  Synchronises with
+        this device; resets the status word."""
+        n = self.failed_waits()
+        if n:
+            self.status.zero_()
+            raise RuntimeError(
+                f"PeerReducer (rank {self.rank} of {self.world}): {n} wait(s) for a peer's partial sums gave "
+                f"up (a rank late by more than the bounded wait, or gone); the weight/bias gradients of the "
+                f"affected call(s) are NaN")
 
     def close(self) -> None:
         """Collective: unmap the peers' buffers, then free this rank's."""
         if self._own is None:
+            return
+        if not self._collective:
+            self._own = None
             return
         rt = self._rt
         torch.cuda.synchronize(self.device)
@@ -225,7 +296,9 @@ def causal_conv1d_fn_batch_sharded(
     weight/bias: weight.grad / bias.grad come out summed over all ranks of
     `group` (the data-parallel gradient), x.grad stays local.  With a
     `reducer` the sum is fused into the backward kernel over NVLink peer
-    memory; otherwise one all-reduce over `group`."""
+    memory (call ``reducer.check()`` before using the gradients, e.g. before
+    the optimizer step, to turn a peer that never arrived into an error);
+    otherwise one all-reduce over `group`."""
     if activation not in (None, "silu", "swish"):
         raise NotImplementedError("only activation in {None, 'silu', 'swish'} is supported")
     batch, dim, _ = x.shape

@@ -298,7 +298,7 @@ int bwd_impl(const cc1d_bwd_params* p, const cc1d_peer_reduce* peer, void* strea
     if (e != cudaSuccess) return cuda_fail(e, "cc1d_bwd finalize launch");
   } else {
     PeerFinalizeArgs pf{f, peer->rank, peer->world, peer->exchange, peer->epochs, peer_blocks(p->dim, p->width),
-                        peer->max_polls != 0 ? peer->max_polls : 4194304u};
+                        peer->max_polls != 0 ? peer->max_polls : 4194304u, peer->status};
     e = launch_finalize_peer(p->dtype, p->width, pf, s);
     if (e != cudaSuccess) return cuda_fail(e, "cc1d_bwd_peer_reduce finalize launch");
   }

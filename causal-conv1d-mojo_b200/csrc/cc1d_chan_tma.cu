@@ -130,18 +130,23 @@ __global__ void __launch_bounds__(kThreadsTma, CC1D_FWD_MIN_BLOCKS) fwd_chan_tma
     if (lane == 0) {
       prefetch_tensormap(&p.map_x);
       unsigned k = 0;
-      for (i64 r = cr0; r < cr1;) {
+      bool live = true;
+      for (i64 r = cr0; r < cr1 && live;) {
         const i64 b = r / a.L;
         const i64 t0 = r - b * a.L;
         const i64 t1 = min(a.L, t0 + (cr1 - r));
         r += t1 - t0;
         for (i64 t = t0; t < t1; t += TR, ++k) {
           const unsigned s = k % kFwdStages, use = k / kFwdStages;
-          if (use > 0 && !mbar_wait(&empty[s], (use - 1) & 1)) return;
+          if (use > 0 && !mbar_wait(&empty[s], (use - 1) & 1)) {
+            live = false;  // consumers stopped: issue nothing more
+            break;
+          }
           mbar_arrive_expect_tx(&full[s], STAGE_BYTES);
           tma_load_3d(smem + s * STAGE_BYTES, &p.map_x, &full[s], (int)c0, (int)t, (int)b);
         }
       }
+      mbar_drain(full, k, kFwdStages);
     }
     return;
   }
@@ -393,7 +398,8 @@ __global__ void __launch_bounds__(kThreadsTma, CC1D_BWD_MIN_BLOCKS) bwd_chan_tma
       prefetch_tensormap(&p.map_x);
       prefetch_tensormap(&p.map_g);
       unsigned k = 0;
-      for (i64 r = cr0; r < cr1;) {
+      bool live = true;
+      for (i64 r = cr0; r < cr1 && live;) {
         const i64 b = r / a.L;
         const i64 t0 = r - b * a.L;
         const i64 t1 = min(a.L, t0 + (cr1 - r));
@@ -401,13 +407,17 @@ __global__ void __launch_bounds__(kThreadsTma, CC1D_BWD_MIN_BLOCKS) bwd_chan_tma
         const i64 tl = min(a.L, t1 + H);  // dx of the last rows needs H rows more
         for (i64 t = t0; t < tl; t += TR, ++k) {
           const unsigned s = k % kBwdStages, use = k / kBwdStages;
-          if (use > 0 && !mbar_wait(&empty[s], (use - 1) & 1)) return;
+          if (use > 0 && !mbar_wait(&empty[s], (use - 1) & 1)) {
+            live = false;  // consumers stopped: issue nothing more
+            break;
+          }
           mbar_arrive_expect_tx(&full[s], STAGE_BYTES);
           unsigned char* dst = smem + s * STAGE_BYTES;
           tma_load_3d(dst, &p.map_x, &full[s], (int)c0, (int)t, (int)b);
           tma_load_3d(dst + TILE_BYTES, &p.map_g, &full[s], (int)c0, (int)t, (int)b);
         }
       }
+      mbar_drain(full, k, kBwdStages);
     }
     return;
   }

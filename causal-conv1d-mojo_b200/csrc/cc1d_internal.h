@@ -80,6 +80,7 @@ struct PeerFinalizeArgs {
   uint32_t* epochs;                 // this rank's per-block call counters (nblocks)
   i64 nblocks;
   unsigned max_polls;               // bounded wait per peer word
+  uint32_t* status;                 // optional: +1 per warp whose wait gave up
 };
 
 struct UpdateArgs {

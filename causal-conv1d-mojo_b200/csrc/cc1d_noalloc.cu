@@ -60,10 +60,17 @@ extern "C" int cc1d_bwd_noalloc(const cc1d_bwd_params* params, void* stream) {
                               "cc1d_bwd_noalloc: this call needs %zu bytes of scratch but the built-in scratch "
                               "holds %zu bytes; use cc1d_bwd with a caller-provided workspace",
                               need, (size_t)CC1D_NOALLOC_SCRATCH_BYTES);
-  void* scratch = nullptr;
-  rc = scratch_address(&scratch);
-  if (rc != CC1D_OK) return rc;
-  p.workspace = scratch;
-  p.workspace_bytes = CC1D_NOALLOC_SCRATCH_BYTES;
+  if (need > 0) {
+    // cc1d_bwd_workspace_size made the device holding the data current on
+    // this thread (it does so whenever the call has work, i.e. need > 0),
+    // so the symbol address is that device's copy of the array.  Calls with
+    // nothing to reduce take no scratch and never look it up: they cannot
+    // touch, or cache the address on, whatever device happens to be current.
+    void* scratch = nullptr;
+    rc = scratch_address(&scratch);
+    if (rc != CC1D_OK) return rc;
+    p.workspace = scratch;
+    p.workspace_bytes = CC1D_NOALLOC_SCRATCH_BYTES;
+  }
   return cc1d_bwd(&p, stream);
 }

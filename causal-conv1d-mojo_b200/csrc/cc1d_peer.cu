@@ -11,7 +11,9 @@
 //      selected by the call's parity),
 //   2. polls its own exchange buffer until the words of every rank carry
 //      this call's tag (bounded wait), then adds the ranks' values in rank
-//      order and writes fp32 dwdb plus the parameter-dtype copies.
+//      order and writes fp32 dwdb plus the parameter-dtype copies.  A wait
+//      that gives up writes NaN to the outputs it could not reduce and adds
+//      1 to the caller's status word (and to the process-wide counter).
 // An aligned 8-byte store is seen whole or not at all, so value and tag
 // travel together: no fences, no flags, no remote loads; the exchange costs
 // one NVLink store latency.  The halves alternate by call parity, and a rank
@@ -105,8 +107,15 @@ __global__ void __launch_bounds__(kPeerWarps * 32) finalize_peer_kernel(const Pe
         t += __uint_as_float((unsigned)(w & 0xffffffffull));
       }
     }
-    if (__any_sync(kFull, active && !ok) && lane == 0) atomicAdd(&g_peer_timeouts, 1u);
-    if (!active || !ok) continue;  // a timed-out output stays unwritten
+    if (__any_sync(kFull, active && !ok) && lane == 0) {
+      atomicAdd(&g_peer_timeouts, 1u);
+      if (p.status != nullptr) atomicAdd(p.status, 1u);
+    }
+    if (!active) continue;
+    // An output whose exchange timed out is written as NaN (never left
+    // stale): a caller that skips the status check still sees the failure
+    // in the gradients instead of silently training on garbage.
+    if (!ok) t = __uint_as_float(0x7fc00000u);
     const i64 c = e / (W + 1);
     const int k = (int)(e - c * (W + 1));
     if (k < W) {

@@ -260,11 +260,12 @@ __global__ void __launch_bounds__(kThreadsSeq, CC1D_SEQ_FWD_MIN_BLOCKS) fwd_seq_
       unsigned k = 0;
       for (i64 t = t0; t < t1; t += kTL, ++k) {
         const unsigned s = k % NS, use = k / NS;
-        if (use > 0 && !mbar_wait(&empty[s], (use - 1) & 1)) return;
+        if (use > 0 && !mbar_wait(&empty[s], (use - 1) & 1)) break;  // consumers stopped
         mbar_arrive_expect_tx(&full[s], SB);
         tma_load_3d(smem + s * SB, &p.map_x, &full[s], (int)t, (int)c0, (int)b);
         if (HAS_SEQ) tma_load_3d(smem + s * SB + TB, &p.map_s, &full[s], (int)t, 0, (int)b);
       }
+      mbar_drain(full, k, NS);
     }
     return;
   }
@@ -471,12 +472,13 @@ __global__ void __launch_bounds__(kThreadsSeq, W > 5 ? 1 : (HAS_SEQ ? CC1D_SEQ_B
       unsigned k = 0;
       for (i64 t = t0; t < t1; t += kTL, ++k) {
         const unsigned s = k % NS, use = k / NS;
-        if (use > 0 && !mbar_wait(&empty[s], (use - 1) & 1)) return;
+        if (use > 0 && !mbar_wait(&empty[s], (use - 1) & 1)) break;  // consumers stopped
         mbar_arrive_expect_tx(&full[s], SB);
         tma_load_3d(smem + s * SB, &p.map_x, &full[s], (int)t, (int)c0, (int)b);
         tma_load_3d(smem + s * SB + TB, &p.map_g, &full[s], (int)t, (int)c0, (int)b);
         if (HAS_SEQ) tma_load_3d(smem + s * SB + 2 * TB, &p.map_s, &full[s], (int)t, 0, (int)b);
       }
+      mbar_drain(full, k, NS);
     }
     return;
   }
@@ -848,12 +850,14 @@ __global__ void __launch_bounds__(kThreadsSeq, CC1D_SEQ_FWD_SH_MIN_BLOCKS) fwd_s
     if (lane == 0) {
       prefetch_tensormap(&p.map_x);
       const i64 rbase = b * a.xs_b + c0 * a.xs_c;
-      for (int k = 0; k < ntiles; ++k) {
+      int k = 0;
+      for (; k < ntiles; ++k) {
         const unsigned s = k % NS, use = k / NS;
-        if (use > 0 && !mbar_wait(&empty[s], (use - 1) & 1)) return;
+        if (use > 0 && !mbar_wait(&empty[s], (use - 1) & 1)) break;  // consumers stopped
         mbar_arrive_expect_tx(&full[s], p.sg.tx);
         shift_load_rows(smem + s * SB, RB, &p.map_x, &full[s], rbase, a.xs_c, t0 + k * kTL, E, p.sg.in_log2);
       }
+      mbar_drain(full, (unsigned)k, NS);
     }
     return;
   }
@@ -1025,14 +1029,16 @@ __global__ void __launch_bounds__(kThreadsSeq, W > 5 ? 1 : CC1D_SEQ_BWD_SH_MIN_B
       prefetch_tensormap(&p.map_x);
       prefetch_tensormap(&p.map_g);
       const i64 rbase = b * a.xs_b + c0 * a.xs_c;  // dout and dx have x's strides
-      for (int k = 0; k < ntiles; ++k) {
+      int k = 0;
+      for (; k < ntiles; ++k) {
         const unsigned s = k % NS, use = k / NS;
-        if (use > 0 && !mbar_wait(&empty[s], (use - 1) & 1)) return;
+        if (use > 0 && !mbar_wait(&empty[s], (use - 1) & 1)) break;  // consumers stopped
         mbar_arrive_expect_tx(&full[s], 2 * p.sg.tx);
         const int t = t0 + k * kTL;
         shift_load_rows(smem + s * SB, RB, &p.map_x, &full[s], rbase, a.xs_c, t, E, p.sg.in_log2);
         shift_load_rows(smem + s * SB + TB, RB, &p.map_g, &full[s], rbase, a.xs_c, t, E, p.sg.in_log2);
       }
+      mbar_drain(full, (unsigned)k, NS);
     }
     return;
   }

@@ -81,6 +81,22 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, unsigned parity) {
   return false;
 }
 
+// Producer epilogue of a `stages`-deep ring into which `issued` stage loads
+// were issued (stage k % stages, phase k / stages): waits, bounded, for the
+// last min(issued, stages) of them to land.  In the normal flow they have
+// landed or are about to (the consumers wait for the same phases).  After a
+// wait gave up -- the consumers may have returned -- it keeps this block
+// resident until its bulk copies stop writing its shared memory, so no
+// block exits with async copies still in flight.  Stops at the first wait
+// that gives up (counted like any other).
+__device__ __forceinline__ void mbar_drain(uint64_t* full, unsigned issued, unsigned stages) {
+  const unsigned n = issued < stages ? issued : stages;
+  for (unsigned i = 1; i <= n; ++i) {
+    const unsigned k = issued - i;
+    if (!mbar_wait(&full[k % stages], (k / stages) & 1)) return;
+  }
+}
+
 // 3-D tiled TMA load into shared memory, completion signalled on `bar`.
 __device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, uint64_t* bar, int x, int y, int z) {
   asm volatile(

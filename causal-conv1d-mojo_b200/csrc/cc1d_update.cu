@@ -26,9 +26,10 @@
 // programmatic dependent launch (waits on griddepcontrol before touching
 // memory).
 //
-// varlen_states_kernel: one thread per (sequence, slot, channel), channel
-// fastest, so reads of x rows and writes of the (batch, state_len, dim)
-// output storage are both coalesced
+// varlen_states_kernel: one thread per (sequence, slot, channel) on a 3-D
+// grid (channel blocks, slot, sequence), channel fastest, so reads of x rows
+// and writes of the (batch, state_len, dim) output storage are both
+// coalesced and no thread divides an index
 // (src/causal_conv1d_mojo/causal_conv1d_varlen.py:29-61).
 #include "cc1d_dispatch.cuh"
 
@@ -574,23 +575,36 @@ __global__ void __launch_bounds__(128, CC1D_CIRC_MIN_BLOCKS) update_circ_row_ker
   }
 }
 
+// One state slot of one sequence: states[i, c, j] for the channels of this
+// block.  Grid (channel blocks, slot j, sequence i): no index division.
 template <typename T>
-__global__ void varlen_states_kernel(const VarlenArgs a) {
+__device__ __forceinline__ void varlen_slot(const VarlenArgs& a, i64 i, i64 j, i64 c) {
+  const i64 beg = a.cu[i];
+  const i64 end = a.cu[i + 1];
+  const i64 start = max(beg, end - a.S);
+  const i64 cnt = end - start;
+  T v = Cvt<T>::to(0.f);
+  const i64 tok = end - a.S + j;
+  if (cnt > 0 && j >= a.S - cnt && tok >= 0 && tok < a.total_tokens)
+    v = static_cast<const T*>(a.x)[tok * a.xs_t + c * a.xs_c];
+  static_cast<T*>(a.st)[i * a.ss_b + c * a.ss_c + j * a.ss_l] = v;
+}
+
+template <typename T>
+__global__ void __launch_bounds__(256) varlen_states_kernel(const VarlenArgs a) {
+  griddep_wait();  // x and cu_seqlens may come from the previous kernel
+  griddep_launch_dependents();
+  const i64 c = (i64)blockIdx.x * blockDim.x + threadIdx.x;
+  if (c < a.D) varlen_slot<T>(a, blockIdx.z, blockIdx.y, c);
+}
+
+// More sequences or slots than a grid's y/z extent: flat index (divisions).
+template <typename T>
+__global__ void varlen_states_flat_kernel(const VarlenArgs a) {
   const i64 n = a.B * a.S * a.D;
   for (i64 e = (i64)blockIdx.x * blockDim.x + threadIdx.x; e < n; e += (i64)gridDim.x * blockDim.x) {
-    const i64 c = e % a.D;
     const i64 bj = e / a.D;
-    const i64 j = bj % a.S;
-    const i64 i = bj / a.S;
-    const i64 beg = a.cu[i];
-    const i64 end = a.cu[i + 1];
-    const i64 start = max(beg, end - a.S);
-    const i64 cnt = end - start;
-    T v = Cvt<T>::to(0.f);
-    const i64 tok = end - a.S + j;
-    if (cnt > 0 && j >= a.S - cnt && tok >= 0 && tok < a.total_tokens)
-      v = static_cast<const T*>(a.x)[tok * a.xs_t + c * a.xs_c];
-    static_cast<T*>(a.st)[i * a.ss_b + c * a.ss_c + j * a.ss_l] = v;
+    varlen_slot<T>(a, bj / a.S, bj % a.S, e - bj * a.D);
   }
 }
 
@@ -718,11 +732,20 @@ cudaError_t launch_varlen_states(int dtype, const VarlenArgs& a, cudaStream_t st
   const i64 n = a.B * a.S * a.D;
   if (n == 0) return cudaSuccess;
   const int threads = 256;
+  if (a.B <= 65535 && a.S <= 65535 && ceil_div(a.D, (i64)threads) <= 0x7fffffffLL) {
+    const dim3 grid((unsigned)ceil_div(a.D, (i64)threads), (unsigned)a.S, (unsigned)a.B);
+    switch (dtype) {
+      case 0: return launch_pdl(varlen_states_kernel<__half>, grid, dim3(threads), 0, stream, a);
+      case 1: return launch_pdl(varlen_states_kernel<__nv_bfloat16>, grid, dim3(threads), 0, stream, a);
+      case 2: return launch_pdl(varlen_states_kernel<float>, grid, dim3(threads), 0, stream, a);
+      default: return cudaErrorInvalidValue;
+    }
+  }
   const unsigned blocks = (unsigned)std::min<i64>(ceil_div(n, threads), 1 << 20);
   switch (dtype) {
-    case 0: varlen_states_kernel<__half><<<blocks, threads, 0, stream>>>(a); break;
-    case 1: varlen_states_kernel<__nv_bfloat16><<<blocks, threads, 0, stream>>>(a); break;
-    case 2: varlen_states_kernel<float><<<blocks, threads, 0, stream>>>(a); break;
+    case 0: varlen_states_flat_kernel<__half><<<blocks, threads, 0, stream>>>(a); break;
+    case 1: varlen_states_flat_kernel<__nv_bfloat16><<<blocks, threads, 0, stream>>>(a); break;
+    case 2: varlen_states_flat_kernel<float><<<blocks, threads, 0, stream>>>(a); break;
     default: return cudaErrorInvalidValue;
   }
   return cudaGetLastError();

@@ -30,7 +30,7 @@
 extern "C" {
 #endif
 
-#define CC1D_ABI_VERSION 1
+#define CC1D_ABI_VERSION 2
 
 #if defined(__GNUC__)
 #define CC1D_API __attribute__((visibility("default")))
@@ -143,15 +143,20 @@ CC1D_API int cc1d_bwd(const cc1d_bwd_params* params, void* stream);
  * the first call, advanced on the device by every call (so the call may be
  * captured in a CUDA graph and replayed).  All ranks must issue the same
  * sequence of calls with the same dim and W, one rank per GPU.  Waits for
- * peers are bounded; a wait that gives up leaves its outputs unwritten and
- * is counted by cc1d_device_status.
+ * peers are bounded.  A wait that gives up (a peer that is late by more than
+ * max_polls polls, or gone) writes NaN into the dwdb_acc / dweight_out /
+ * dbias_out elements it could not reduce -- never stale values -- adds 1 to
+ * *status (when given) and to the count cc1d_device_status reports.  The
+ * call numbers still advance, so the ranks stay in step for the next call.
  */
 typedef struct cc1d_peer_reduce {
   int32_t rank, world;                 /* world <= 32 */
   unsigned long long* const* exchange; /* device array [world] */
   uint32_t* epochs;                    /* this rank's counters */
   uint32_t max_polls;                  /* polls per wait before giving up; 0 = 4194304 (seconds) */
-  uint32_t reserved;
+  uint32_t reserved;                   /* must be 0 */
+  uint32_t* status;                    /* device word, or NULL: +1 per wait that gave up (the caller
+                                          zeroes it and reads it at a sync point of its choosing) */
 } cc1d_peer_reduce;
 
 CC1D_API int64_t cc1d_peer_blocks(int64_t dim, int32_t width);
@@ -167,9 +172,11 @@ CC1D_API int cc1d_bwd_peer_reduce(const cc1d_bwd_params* params, const cc1d_peer
  * device array of CC1D_NOALLOC_SCRATCH_BYTES built into the library, which
  * every GPU that loads the library holds until the process exits.  Calls
  * needing more scratch than that (see cc1d_bwd_workspace_size) fail with
- * CC1D_ERR_WORKSPACE.  The first call on a device looks up the array's
- * device address (make it before any stream capture).  All calls share the
- * array: calls that overlap on the GPU race.  No allocation is made.
+ * CC1D_ERR_WORKSPACE.  The first call on a device that has something to
+ * reduce looks up the array's device address on the device holding the data
+ * (make it before any stream capture); calls on empty problems use no
+ * scratch and make no lookup.  All calls share the array: calls that
+ * overlap on the GPU race.  No allocation is made.
  * No counterpart in the reference (its backward allocates through torch).
  */
 #define CC1D_NOALLOC_SCRATCH_BYTES (16u * 1024u * 1024u)
@@ -228,9 +235,12 @@ typedef struct cc1d_varlen_states_params {
 CC1D_API int cc1d_varlen_states(const cc1d_varlen_states_params* params, void* stream);
 
 /* Diagnostics: *wait_timeouts receives the number of bounded in-kernel waits
- * (pipeline barriers) that gave up since the previous call, on the current
- * device, and the count is reset.  A non-zero count means some results of
- * the kernels launched meanwhile are invalid.  Synchronises the device.
+ * (pipeline barriers, peer exchanges) that gave up since the previous call,
+ * and the count is reset.  The count is kept per device and this call reads
+ * the CURRENT device's only: a process that drives several GPUs makes each
+ * one current in turn (cudaSetDevice) and calls it once per device.  A
+ * non-zero count means some results of the kernels launched meanwhile on
+ * that device are invalid.  Synchronises that device.
  * No reference counterpart (the reference kernels have no in-kernel waits). */
 CC1D_API int cc1d_device_status(unsigned* wait_timeouts);
 

@@ -48,7 +48,7 @@ def test_library_exports_nothing_else():
 def test_version_and_abi():
     lib = _lib.load()
     assert lib.cc1d_version().decode() == "1.6.1"
-    assert lib.cc1d_abi_version() == 1
+    assert lib.cc1d_abi_version() == 2
     assert lib.cc1d_last_error() is not None
 
 

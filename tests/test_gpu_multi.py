@@ -154,6 +154,7 @@ def _run_case(case, rank, world, dev):
         if ba is not None:
             torch.testing.assert_close(ba.grad.float(), bf.grad.float(), rtol=tol["rtol"], atol=tol["atol"] * 10)
         torch.cuda.synchronize(dev)
+        reducer.check()  # no wait for a peer gave up
         assert _lib.device_wait_timeouts() == 0
     finally:
         reducer.close()
@@ -257,7 +258,7 @@ def test_peer_wait_gives_up_and_reports():
     dwdb = torch.full((D * (W + 1),), float("nan"), device=dev)
     dw = torch.full((D, W), float("nan"), dtype=torch.bfloat16, device=dev)
     db = torch.full((D,), float("nan"), dtype=torch.bfloat16, device=dev)
-    _ops.bwd_peer(x, w, b, dout, init, None, dx, dwdb, dinit, dw, db, True, ptrs, epochs, 0, 2, 1024)
+    _ops.bwd_peer(x, w, b, dout, init, None, dx, dwdb, dinit, dw, db, True, ptrs, epochs, 0, 2, 1024, None)
     torch.cuda.synchronize(dev)
     assert _lib.device_wait_timeouts() > 0
     assert torch.isnan(dwdb).all() and torch.isnan(dw).all() and torch.isnan(db).all()
@@ -271,8 +272,43 @@ def test_peer_wait_gives_up_and_reports():
     one = torch.zeros_like(own)
     _ops.bwd_peer(x, w, b, dout, init, None, dx, dwdb, dinit, dw, db, True,
                   torch.tensor([one.data_ptr()], dtype=torch.int64, device=dev),
-                  torch.zeros(nblocks, dtype=torch.int32, device=dev), 0, 1)
+                  torch.zeros(nblocks, dtype=torch.int32, device=dev), 0, 1, 0, None)
     torch.cuda.synchronize(dev)
     assert _lib.device_wait_timeouts() == 0
     assert torch.equal(dwdb, ref_dwdb)
     assert torch.equal(dw, ref_dwdb[: D * W].view(D, W).to(torch.bfloat16))
+
+
+def test_batch_sharded_autograd_raises_when_a_peer_never_arrives():
+    """The autograd path with a reducer whose second 'rank' never pushes (a
+    buffer nobody writes, one GPU, no fault): the bounded waits give up, the
+    weight/bias gradients come out NaN (never stale memory), the reducer's
+    status word counts the failure and check() raises; after that the
+    status is clear again."""
+    from causal_conv1d_b200 import _lib
+    from causal_conv1d_b200.parallel import PeerReducer, causal_conv1d_fn_batch_sharded
+
+    dev = torch.device("cuda", 0)
+    B, D, L, W = 2, 256, 64, 4
+    x, w, b, init, douts = _case_inputs(torch.bfloat16, B, D, L, W, 13, True, True)
+    lib = _lib.load()
+    n_words = int(lib.cc1d_peer_exchange_bytes(D, W, 2)) // 8
+    own = torch.zeros(n_words, dtype=torch.int64, device=dev)
+    silent = torch.zeros_like(own)
+    ptrs = torch.tensor([own.data_ptr(), silent.data_ptr()], dtype=torch.int64, device=dev)
+    reducer = PeerReducer.from_exchange(ptrs, rank=0, dim=D, width=W, max_polls=1024)
+    _lib.device_wait_timeouts(dev)  # reset the process-wide count
+    xa = x.to(dev).requires_grad_()
+    wa = w.to(dev).requires_grad_()
+    ba = b.to(dev).requires_grad_()
+    out = causal_conv1d_fn_batch_sharded(xa, wa, ba, activation="silu", reducer=reducer)
+    out.backward(douts[0].to(dev))
+    torch.cuda.synchronize(dev)
+    assert torch.isnan(wa.grad).all() and torch.isnan(ba.grad).all()
+    assert torch.isfinite(xa.grad).all()  # dx does not depend on the exchange
+    assert reducer.failed_waits() > 0
+    with pytest.raises(RuntimeError, match="gave up"):
+        reducer.check()
+    reducer.check()  # the status word was reset by the failed check
+    assert _lib.device_wait_timeouts(dev) > 0
+    reducer.close()
