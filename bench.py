@@ -307,9 +307,16 @@ def time_c2(args, world, rank, reducer):
         # Each rank's step with a local reduction only (no exchange, no
         # waiting for peers): the spread of these is the GPUs' own speed
         # difference, which a synchronous data-parallel step cannot hide.
+        # The fused step's results (dwdb, dw, db hold the cross-rank sums)
+        # are checked first; the local-reduction step below writes its own
+        # buffers, so it cannot disturb them either way.
+        extra["parity"] = peer_parity(x, w, b, dout, init, dwdb, dw, db, world)
+        l_dx, l_dinit = torch.empty_like(dx), torch.empty_like(dinit)
+        l_dwdb, l_dw, l_db = torch.empty_like(dwdb), torch.empty_like(dw), torch.empty_like(db)
+
         def local_step(_=0):
             fwd()
-            _ops.bwd(x, w, b, dout, None, init, None, dx, dwdb, dinit, dw, db, True)
+            _ops.bwd(x, w, b, dout, None, init, None, l_dx, l_dwdb, l_dinit, l_dw, l_db, True)
 
         local_ms = graph_ms(graph_of(local_step, 10), reps, 10)
         per_rank = gather_floats([total_ms / K, bwd_ms, local_ms], world)
@@ -320,7 +327,6 @@ def time_c2(args, world, rank, reducer):
             "note": "step_local_reduction_ms: the same fwd+bwd with the dweight/dbias reduction kept on the "
                     "rank (no exchange); its max over ranks bounds a synchronous step from below",
         }
-        extra["parity"] = peer_parity(x, w, b, dout, init, dwdb, dw, db, world)
     extra["parity_c2"] = c2_parity(x, w, b, init, dout, out, fs, dx, dinit, dw, db) if rank == 0 else None
     total_ms = max_over_ranks(total_ms, world)
     return dict(ms_per_step=total_ms / K, fwd_ms=fwd_ms, bwd_ms=bwd_ms, clocks=clk.summary(), **extra)

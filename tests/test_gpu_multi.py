@@ -160,6 +160,57 @@ def _run_case(case, rank, world, dev):
         reducer.close()
 
 
+def _run_dim_shard(rank, world, dev):
+    """Dim sharding ('sharded over dim'): rank r runs
+    causal_conv1d_fn on its channel slice -- a view of the channel-last
+    (Mamba-layout) activations with the matching weight / bias / state
+    slices -- with no collective at all.  The slices are gathered afterwards
+    only to check them: out, final_states, dx and dinitial_states must equal
+    the unsharded single-GPU result bitwise (rows (b, c) are independent and
+    every kernel evaluates a row with the same arithmetic), dweight / dbias
+    within the fp32 reduction tolerance (the partial-sum split depends on the
+    number of channels).  Channel slices as the reference's
+    tests/test_noncontig_layouts.py:28-43."""
+    import torch.distributed as dist
+
+    from causal_conv1d_b200 import causal_conv1d_fn
+    from causal_conv1d_b200.parallel import dim_shard
+
+    dtype, B, D, L, W = torch.bfloat16, 2, 1024, 512, 4
+    x, w, b, init, douts = _case_inputs(dtype, B, D, L, W, 77, True, True)
+    ws, bs, (d0, d1) = dim_shard(w, b, rank, world)
+    # Every rank holds the full activations in this test; its shard is a
+    # channel-slice VIEW (no copy), as a model that shards channels would pass.
+    xf, dof = x.to(dev), douts[0].to(dev)
+    xs = xf[:, d0:d1].detach().requires_grad_()
+    wsd = ws.to(dev).requires_grad_()
+    bsd = bs.to(dev).requires_grad_()
+    isd = init[:, d0:d1].to(dev).requires_grad_()
+    out, fs = causal_conv1d_fn(xs, wsd, bsd, initial_states=isd, return_final_states=True, activation="silu")
+    out.backward(dof[:, d0:d1])
+    torch.cuda.synchronize(dev)
+    # Reference: the unsharded problem on this GPU.
+    xa = xf.detach().requires_grad_()
+    wa = w.to(dev).requires_grad_()
+    ba = b.to(dev).requires_grad_()
+    ia = init.to(dev).requires_grad_()
+    outa, fsa = causal_conv1d_fn(xa, wa, ba, initial_states=ia, return_final_states=True, activation="silu")
+    outa.backward(dof)
+    torch.cuda.synchronize(dev)
+    tag = f"dim shard rank {rank} channels [{d0}, {d1})"
+    assert torch.equal(out, outa[:, d0:d1]), tag + " out"
+    assert torch.equal(fs, fsa[:, d0:d1]), tag + " final_states"
+    assert torch.equal(xs.grad, xa.grad[:, d0:d1]), tag + " dx"
+    assert torch.equal(isd.grad, ia.grad[:, d0:d1]), tag + " dinitial_states"
+    torch.testing.assert_close(wsd.grad.float(), wa.grad[d0:d1].float(), rtol=1e-2, atol=1e-2)
+    torch.testing.assert_close(bsd.grad.float(), ba.grad[d0:d1].float(), rtol=1e-2, atol=1e-2)
+    # The shards tile the channels: gathered slice bounds cover [0, D).
+    bounds = [None] * world
+    dist.all_gather_object(bounds, (d0, d1))
+    assert bounds[0][0] == 0 and bounds[-1][1] == D
+    assert all(bounds[r][1] == bounds[r + 1][0] for r in range(world - 1))
+
+
 def _worker(rank, world, port, q):
     sys.path[:0] = [str(REPO), str(REPO / "causal-conv1d-mojo_b200")]
     os.environ["MASTER_ADDR"] = "127.0.0.1"
@@ -174,6 +225,8 @@ def _worker(rank, world, port, q):
     try:
         for case in CASES:
             _run_case(case, rank, world, dev)
+        case = "dim shard"
+        _run_dim_shard(rank, world, dev)
         q.put((rank, "ok", ""))
     except Exception:  # reported to the parent
         q.put((rank, "fail", f"case {case}\n" + traceback.format_exc()))
@@ -182,7 +235,7 @@ def _worker(rank, world, port, q):
 
 
 @pytest.mark.skipif(WORLD < 2, reason="needs two or more GPUs")
-def test_peer_reduce_matches_rank_order_sum():
+def test_peer_reduce_and_dim_shard_match_single_gpu():
     import torch.multiprocessing as mp
 
     ctx = mp.get_context("spawn")
