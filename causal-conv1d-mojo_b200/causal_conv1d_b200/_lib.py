@@ -96,6 +96,22 @@ class VarlenParams(ctypes.Structure):
     ]
 
 
+class InprojConvParams(ctypes.Structure):
+    _fields_ = [
+        ("dtype", c_i32), ("width", c_i32), ("batch", c_i64), ("seqlen", c_i64), ("dim", c_i64),
+        ("hidden_dim", c_i64), ("silu", c_i32), ("_pad0", c_i32),
+        ("hidden", c_ptr), ("hidden_row_stride", c_i64),
+        ("in_weight", c_ptr), ("in_weight_row_stride", c_i64),
+        ("conv_weight", c_ptr), ("conv_weight_dim_stride", c_i64), ("conv_weight_width_stride", c_i64),
+        ("conv_bias", c_ptr), ("conv_bias_stride", c_i64),
+        ("initial_states", c_ptr), ("init_batch_stride", c_i64), ("init_dim_stride", c_i64),
+        ("init_seq_stride", c_i64),
+        ("out", c_ptr), ("out_row_stride", c_i64),
+        ("final_states", c_ptr), ("final_batch_stride", c_i64), ("final_dim_stride", c_i64),
+        ("final_seq_stride", c_i64),
+    ]
+
+
 class PeerReduceParams(ctypes.Structure):
     _fields_ = [("rank", c_i32), ("world", c_i32), ("exchange", c_ptr), ("epochs", c_ptr),
                 ("max_polls", ctypes.c_uint32), ("reserved", ctypes.c_uint32), ("status", c_ptr)]
@@ -112,6 +128,7 @@ SIGNATURES = {
     "cc1d_peer_exchange_bytes": (c_i64, [c_i64, c_i32, c_i32]),
     "cc1d_update": (c_i32, [ctypes.POINTER(UpdateParams), c_ptr]),
     "cc1d_varlen_states": (c_i32, [ctypes.POINTER(VarlenParams), c_ptr]),
+    "cc1d_inproj_conv_fwd": (c_i32, [ctypes.POINTER(InprojConvParams), c_ptr]),
     "cc1d_device_status": (c_i32, [ctypes.POINTER(ctypes.c_uint)]),
     "cc1d_last_error": (ctypes.c_char_p, []),
     "cc1d_version": (ctypes.c_char_p, []),

@@ -332,3 +332,54 @@ def _varlen_fake(x, cu_seqlens, states) -> None:
 
 varlen_states = torch.library.custom_op("causal_conv1d_b200::varlen_states", mutates_args=("states",))(_varlen_impl)
 varlen_states.register_fake(_varlen_fake)
+
+
+def _inproj_conv_impl(
+    hidden: torch.Tensor,
+    in_weight: torch.Tensor,
+    conv_weight: torch.Tensor,
+    conv_bias: torch.Tensor | None,
+    initial_states: torch.Tensor | None,
+    out: torch.Tensor,
+    apply_silu: bool,
+    final_states_out: torch.Tensor | None,
+) -> None:
+    """out (B, L, N) = conv(hidden (B, L, K) @ in_weight (N, K)^T) in one kernel
+    (cc1d_inproj_conv_fwd); final_states_out (B, N, W-1) optional."""
+    _require_cuda(hidden, "in_proj_causal_conv1d")
+    lib = _lib.load()
+    B, L, K = hidden.shape
+    N, W = conv_weight.shape
+    p = _lib.InprojConvParams()
+    p.dtype = _DTYPE_CODE[hidden.dtype]
+    p.width = W
+    p.batch, p.seqlen, p.dim, p.hidden_dim = B, L, N, K
+    p.silu = 1 if apply_silu else 0
+    p.hidden = hidden.data_ptr()
+    p.hidden_row_stride = hidden.stride(1)
+    p.in_weight = in_weight.data_ptr()
+    p.in_weight_row_stride = in_weight.stride(0)
+    p.conv_weight = conv_weight.data_ptr()
+    p.conv_weight_dim_stride, p.conv_weight_width_stride = conv_weight.stride()
+    if conv_bias is not None:
+        p.conv_bias, p.conv_bias_stride = conv_bias.data_ptr(), conv_bias.stride(0)
+    if initial_states is not None:
+        p.initial_states = initial_states.data_ptr()
+        p.init_batch_stride, p.init_dim_stride, p.init_seq_stride = initial_states.stride()
+    p.out = out.data_ptr()
+    p.out_row_stride = out.stride(1)
+    if final_states_out is not None:
+        p.final_states = final_states_out.data_ptr()
+        p.final_batch_stride, p.final_dim_stride, p.final_seq_stride = final_states_out.stride()
+    with _on_device(hidden.device):
+        _lib.check(lib.cc1d_inproj_conv_fwd(ctypes.byref(p), _stream(hidden.device)), "cc1d_inproj_conv_fwd")
+
+
+def _inproj_conv_fake(hidden, in_weight, conv_weight, conv_bias, initial_states, out, apply_silu,
+                      final_states_out) -> None:
+    return None
+
+
+inproj_conv = torch.library.custom_op(
+    "causal_conv1d_b200::inproj_conv", mutates_args=("out", "final_states_out"))(_inproj_conv_impl)
+inproj_conv.register_fake(_inproj_conv_fake)

@@ -378,6 +378,8 @@ int cc1d_device_status(unsigned* wait_timeouts) {
   if (e != cudaSuccess) return cuda_fail(e, "cc1d_device_status");
   e = read_peer_timeouts(wait_timeouts);
   if (e != cudaSuccess) return cuda_fail(e, "cc1d_device_status");
+  e = read_fused_aborts(wait_timeouts);
+  if (e != cudaSuccess) return cuda_fail(e, "cc1d_device_status");
   return ok();
 }
 

@@ -146,6 +146,8 @@ i64 peer_blocks(i64 dim, int width);
 i64 peer_exchange_bytes(i64 dim, int width, int world);
 cudaError_t launch_finalize_peer(int dtype, int width, const PeerFinalizeArgs& p, cudaStream_t stream);
 cudaError_t read_peer_timeouts(unsigned* count);
+// Blocks of the fused in_proj + conv kernel that gave up on a bounded wait.
+cudaError_t read_fused_aborts(unsigned* count);
 
 // Records a message for cc1d_last_error() and returns `code` (for entry
 // points defined outside cc1d_abi.cu).

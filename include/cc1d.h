@@ -234,6 +234,44 @@ typedef struct cc1d_varlen_states_params {
 
 CC1D_API int cc1d_varlen_states(const cc1d_varlen_states_params* params, void* stream);
 
+/*
+ * The in_proj GEMM of a Mamba block with the forward conv as its epilogue
+ * (bf16; widths 2..4):
+ *   xBC = hidden (M, K) @ in_weight (N, K)^T, M = batch * seqlen tokens,
+ *   out[m, :] = act(conv_bias + sum_j conv_weight[:, j] * xBC[m - (W-1) + j, :])
+ * with the conv of cc1d_fwd applied to each sequence of seqlen tokens
+ * (initial_states before its start, final_states = its last W-1 xBC rows),
+ * on xBC rounded to bf16 exactly as a stored GEMM output would be.  xBC
+ * itself is never written: out (M, N) is stored token-major, i.e. the
+ * channel-last (batch, dim, seqlen) layout of causal_conv1d_fn.
+ * Requirements: dim % 32 == 0, hidden_dim % 8 == 0, seqlen >= W-1; hidden,
+ * in_weight and out with unit stride along their last dimension and
+ * 16-byte aligned bases and row pitches.  Forward only.
+ *
+ * No counterpart in the reference: it replaces the pair "in_proj GEMM, then
+ * causal_conv1d_fn" that a Mamba block runs, removing the GEMM output's
+ * HBM round trip (src/causal_conv1d_mojo/_fn.py:232 allocates the conv's
+ * output; fwd/kernel.mojo:161-196 reads xBC back).
+ */
+typedef struct cc1d_inproj_conv_params {
+  int32_t dtype;            /* CC1D_BF16 */
+  int32_t width;            /* 2..4 */
+  int64_t batch, seqlen;
+  int64_t dim;              /* N: conv channels = rows of in_weight */
+  int64_t hidden_dim;       /* K */
+  int32_t silu;
+  int32_t _pad0;
+  const void* hidden;       int64_t hidden_row_stride;      /* (M, K) */
+  const void* in_weight;    int64_t in_weight_row_stride;   /* (N, K), as nn.Linear.weight */
+  const void* conv_weight;  int64_t conv_weight_dim_stride, conv_weight_width_stride; /* (N, W) */
+  const void* conv_bias;    int64_t conv_bias_stride;       /* NULL: no bias */
+  const void* initial_states; int64_t init_batch_stride, init_dim_stride, init_seq_stride; /* NULL: zeros */
+  void* out;                int64_t out_row_stride;         /* (M, N) */
+  void* final_states;       int64_t final_batch_stride, final_dim_stride, final_seq_stride; /* NULL: not written */
+} cc1d_inproj_conv_params;
+
+CC1D_API int cc1d_inproj_conv_fwd(const cc1d_inproj_conv_params* params, void* stream);
+
 /* Diagnostics: *wait_timeouts receives the number of bounded in-kernel waits
  * (pipeline barriers, peer exchanges) that gave up since the previous call,
  * and the count is reset.  The count is kept per device and this call reads

@@ -93,6 +93,7 @@ STRUCTS = {
     "cc1d_update_params": _lib.UpdateParams,
     "cc1d_varlen_states_params": _lib.VarlenParams,
     "cc1d_peer_reduce": _lib.PeerReduceParams,
+    "cc1d_inproj_conv_params": _lib.InprojConvParams,
 }
 
 
