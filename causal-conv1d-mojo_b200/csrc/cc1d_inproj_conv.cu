@@ -11,29 +11,46 @@
 // applied to the GEMM's accumulator tile before anything leaves the SM, so
 // xBC is never stored; only out (and final_states) are.
 //
-// Kernel (persistent, one CTA per SM, 6 warps):
-//   warp 0      TMA producer: [128 x 64] tiles of hidden and [256 x 64] tiles
-//               of in_weight (bf16, K-major, 128-byte swizzle) into a
-//               4-stage shared-memory ring (full/empty mbarriers).
-//   warp 1      allocates 512 TMEM columns (two 128 x 256 fp32 accumulators)
-//               and one lane issues tcgen05.mma (M=128, N=256, K=16, bf16 in,
-//               fp32 accumulate) for each stage, committing the stage back to
-//               the producer and, after the last K step, the accumulator to
-//               the epilogue.
-//   warps 2..5  epilogue: tcgen05.ld of 32-column chunks (thread = TMEM lane =
-//               tile row), rounded to bf16 exactly as the unfused GEMM would
-//               store xBC, exchanged through shared memory so that every row
-//               sees the W-1 rows above it, conv + bias + SiLU in fp32 with
-//               the tap order of every other kernel of this library, and
-//               16-byte global stores of the output rows.
+// Kernel: persistent, clusters of two CTAs (one per SM) computing one
+// 256-token x 256-channel tile together with 2-SM MMAs (cta_group::2).
+// CTA c of a pair owns the tile's 128 GEMM rows of M-tile 2*pair_m + c and
+// loads them (A), plus channels [n0 + 128c, n0 + 128c + 128) of in_weight
+// (its half of B); each tcgen05.mma of the pair's leader CTA reads A and B
+// from both CTAs' shared memory and writes each CTA's 128 accumulator rows
+// into that CTA's TMEM.  Per CTA, 6 warps:
+//   warp 0      TMA producer: [128 x 64] tiles of hidden and of in_weight
+//               (bf16, K-major, 128-byte swizzle) into a 6-stage ring; the
+//               loads of both CTAs complete on the leader's "full" barrier.
+//   warp 1      allocates 512 TMEM columns (two 128 x 256 fp32 accumulators,
+//               in both CTAs); in the leader, one lane issues tcgen05.mma
+//               (M=256, N=256, K=16, bf16 in, fp32 accumulate) and commits
+//               each stage back to both CTAs' producers and, after the last
+//               K step, the accumulator to both CTAs' epilogues.
+//   warps 2..9  epilogue, per 128-channel chunk of the accumulator: each
+//               thread reads half of its TMEM lane (= tile row) with
+//               tcgen05.ld, rounds it to bf16 exactly as the unfused GEMM
+//               would store xBC, and writes it to a shared-memory staging
+//               tile; then the roles turn: a thread owns two adjacent
+//               channels and a quarter of the rows, keeps their weights,
+//               bias and W-1 previous inputs in registers and walks the rows
+//               8 at a time (loads first, then 8 independent outputs) with
+//               packed fp32 math (the tap order and SiLU of every other
+//               kernel of this library), each warp storing 128 contiguous
+//               output bytes per row.
 // The two accumulators alternate, so the epilogue of one tile overlaps the
-// MMAs of the next.
+// MMAs of the next.  Per K step a CTA moves 32 KB (its A rows and half of
+// B) for 128 x 256 x 64 MACs: a 128 x 256 tile on one SM moves 48 KB for
+// the same work, and a 256 x 256 tile on one SM needs all of its TMEM for
+// one tile (no overlap).  Measured at the Mamba-2 shape, in order: 485 us
+// (128 x 256, one SM: tensor pipe 32% busy, waiting on TMA), 461 us (256 x
+// 256, one SM), and this design.
 //
-// Halo: the conv of output row m needs xBC rows m-(W-1) .. m.  A tile's 128
-// GEMM rows start W-1 rows before its first output row, so each tile carries
-// its own halo and produces 128-(W-1) output rows (tiles overlap by W-1
-// rows; 2.4% extra MMA work at W = 4).  The first W-1 rows of a tile are
-// computed but not stored.  No multicast loads are used anywhere.
+// Halo: the conv of output row m needs xBC rows m-(W-1) .. m.  A CTA's 128
+// GEMM rows start W-1 rows before its first output row, so each carries its
+// own halo and produces 128-(W-1) output rows (2.4% extra MMA work at
+// W = 4).  The first W-1 rows are computed but not stored.  No TMA load in
+// this file uses cluster multicast; the leader reaches its peer's barriers
+// through mapa addresses.
 //
 // Every mbarrier wait is bounded; a wait that gives up sets a block-wide
 // abort flag, every role stops issuing, waits (bounded) for the copies and
@@ -54,26 +71,24 @@ namespace {
 constexpr int kBM = 128;       // GEMM rows per tile (tokens, halo included)
 constexpr int kBN = 256;       // channels per tile
 constexpr int kBK = 64;        // K per stage: 64 bf16 = one 128-byte swizzle row
-constexpr int kStages = 4;
+constexpr int kStages = 5;
 constexpr int kUmmaK = 16;     // K per tcgen05.mma (kind::f16)
-constexpr int kChunk = 32;     // accumulator columns per epilogue step
-constexpr int kEpiWarps = 4;
+constexpr int kChunk = 128;    // accumulator columns per epilogue step
+constexpr int kEpiWarps = 8;
 constexpr int kThreads = (2 + kEpiWarps) * 32;
 constexpr unsigned kABytes = kBM * kBK * 2;     // 16 KB
-constexpr unsigned kBBytes = kBN * kBK * 2;     // 32 KB
+constexpr unsigned kBBytes = (kBN / 2) * kBK * 2;  // 16 KB: this CTA's half of B
 constexpr unsigned kStageBytes = kABytes + kBBytes;
 constexpr int kYPitch = kChunk * 2 + 16;        // bytes per staged row (padded: conflict-free 16-byte access)
-constexpr unsigned kYBytes = kBM * kYPitch;     // one staged chunk
-constexpr int kTmemCols = 2 * kBN;              // two accumulators
+constexpr unsigned kYBytes = kBM * kYPitch;     // the staged chunk (bf16)
+constexpr int kTmemCols = 2 * kBN;              // two accumulators (in each CTA of the pair)
 
 // Shared-memory map (offsets from a 1024-byte aligned base).
 constexpr unsigned kOffA = 0;
 constexpr unsigned kOffB = kOffA + kStages * kABytes;
 constexpr unsigned kOffY = kOffB + kStages * kBBytes;
-constexpr unsigned kOffCw = kOffY + 2 * kYBytes;                // conv taps + bias of the tile, x2
-constexpr int kCwRows = 5;                                      // up to W = 4 taps, then the bias
-constexpr unsigned kCwFloats = kCwRows * kBN;                   // [tap][channel]
-constexpr unsigned kOffBar = kOffCw + 2 * kCwFloats * 4;
+constexpr unsigned kPairStageBytes = 2 * kStageBytes;           // both CTAs' loads of one stage
+constexpr unsigned kOffBar = kOffY + kYBytes;
 constexpr unsigned kSmemBytes = kOffBar + 256 + 1024;           // barriers, TMEM slot, alignment slack
 static_assert(kSmemBytes <= 232448, "exceeds the 227 KB of shared memory a block may use");
 
@@ -95,32 +110,79 @@ struct alignas(64) FusedParams {
 
 // ---- tcgen05 / TMEM primitives (inline PTX) ----
 
+// TMEM of a CTA pair: the warp of the same index in both CTAs allocates
+// (and later frees) the same columns in both CTAs' TMEM.
 __device__ __forceinline__ void tmem_alloc(uint32_t* slot, int cols) {
-  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(slot)), "r"(cols)
+  asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(slot)), "r"(cols)
                : "memory");
 }
 __device__ __forceinline__ void tmem_relinquish() {
-  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
 }
 __device__ __forceinline__ void tmem_dealloc(uint32_t taddr, int cols) {
-  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(cols) : "memory");
+  asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(cols) : "memory");
+}
+
+__device__ __forceinline__ uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+
+// shared::cluster address of the same shared-memory location in CTA `rank`
+// of this cluster.
+__device__ __forceinline__ uint32_t peer_addr(const void* p, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_u32(p)), "r"(rank));
+  return r;
+}
+
+// All threads of both CTAs (release / acquire: barrier inits, TMEM state).
+__device__ __forceinline__ void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+// Bounded wait, with cluster-scope acquire, for a phase of a barrier that
+// the other CTA of the pair arrives on.
+__device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, unsigned parity) {
+  for (unsigned i = 0; i < kSpinLimit; ++i) {
+    unsigned ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    if (ok) return true;
+  }
+  atomicAdd(&g_cc1d_wait_timeouts, 1u);
+  return false;
+}
+
+// Arrive on an mbarrier given by its shared::cluster address (either CTA).
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t addr) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(addr) : "memory");
 }
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
 
-// Arrives once on `bar` when every tcgen05.mma this thread issued before has
-// completed (its shared-memory operands read, its accumulator written).
-__device__ __forceinline__ void tc_commit(uint64_t* bar) {
-  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
-               : "memory");
+// Arrives once on the mbarrier at shared::cluster address `bar` (in either
+// CTA of the pair) when every 2-SM tcgen05.mma this thread issued before has
+// completed (its shared-memory operands read, its accumulators written).
+__device__ __forceinline__ void tc_commit(uint32_t bar) {
+  asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
 }
 
-// D[tmem] (+)= A[smem] * B[smem]^T, both K-major.
+// 2-SM MMA, issued by the leader CTA: D (256 x N, rows 0..127 in the
+// leader's TMEM, 128..255 in the peer's) (+)= A (rows 0..127 from the
+// leader's shared memory, 128..255 from the peer's, same address) * B^T
+// (N/2 rows from each CTA), both K-major.
 __device__ __forceinline__ void tc_mma(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc, uint32_t acc) {
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
       "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}"
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}"
       ::"r"(tmem_d), "l"(adesc), "l"(bdesc), "r"(idesc), "r"(acc)
       : "memory");
 }
@@ -149,14 +211,16 @@ __device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
 }
 
 // Instruction descriptor, kind::f16: fp32 accumulator, bf16 A and B, both
-// K-major, N = kBN, M = kBM.
+// K-major, N = kBN, M = 2 * kBM (the pair's rows).
 constexpr uint32_t kIdesc = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(kBN >> 3) << 17) |
-                            ((uint32_t)(kBM >> 4) << 24);
+                            ((uint32_t)((2 * kBM) >> 4) << 24);
 
-__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, uint64_t* bar, int x, int y) {
+// 2-D tiled load into this CTA's shared memory whose completion is counted
+// on the mbarrier at shared::cluster address `bar` (the pair leader's).
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, uint32_t bar, int x, int y) {
   asm volatile(
-      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];"
-      ::"r"(smem_u32(dst)), "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(x), "r"(y)
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], "
+      "[%2];" ::"r"(smem_u32(dst)), "l"(reinterpret_cast<uint64_t>(map)), "r"(bar), "r"(x), "r"(y)
       : "memory");
 }
 
@@ -182,21 +246,24 @@ __device__ __forceinline__ bool epi_bar_or(bool pred) {
 __device__ __forceinline__ bool aborted(volatile int* flag) { return *flag != 0; }
 
 template <int W, bool SILU>
-__global__ void __launch_bounds__(kThreads, 1) inproj_conv_kernel(const __grid_constant__ FusedParams p) {
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
+    inproj_conv_kernel(const __grid_constant__ FusedParams p) {
   constexpr int H = W - 1;
   extern __shared__ unsigned char smem_raw[];
   unsigned char* smem = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + kOffBar);
-  uint64_t* empty = full + kStages;
-  uint64_t* tfull = empty + kStages;
-  uint64_t* tempty = tfull + 2;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + kOffBar);  // leader: both CTAs' loads of a stage
+  uint64_t* empty = full + kStages;                               // each CTA: its stage may be refilled
+  uint64_t* tfull = empty + kStages;                              // each CTA: accumulator ready
+  uint64_t* tempty = tfull + 2;                                   // leader: both epilogues drained it
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
-  float* cw_s = reinterpret_cast<float*>(smem + kOffCw);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int num_tiles = p.m_tiles * p.n_tiles;
+  const uint32_t crank = cluster_rank();  // 0: leader (issues the MMAs), 1: peer
+  const bool leader = crank == 0;
+  const int pair = blockIdx.x >> 1, npairs = gridDim.x >> 1;
+  const int num_tiles = p.m_tiles * p.n_tiles;  // pair tiles: (M-tile pair, channel tile)
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) {
@@ -205,7 +272,7 @@ __global__ void __launch_bounds__(kThreads, 1) inproj_conv_kernel(const __grid_c
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&tfull[a], 1);
-      mbar_init(&tempty[a], kEpiWarps);
+      mbar_init(&tempty[a], 2 * kEpiWarps);
     }
     *abort_flag = 0;
     fence_mbar_init();
@@ -214,44 +281,49 @@ __global__ void __launch_bounds__(kThreads, 1) inproj_conv_kernel(const __grid_c
     tmem_alloc(tmem_slot, kTmemCols);
     tmem_relinquish();
   }
+  __syncwarp();
   tc_fence_before();
-  __syncthreads();
+  cluster_sync();  // both CTAs' barriers initialised, TMEM allocated
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
 
   if (warp == 0) {
-    // ---------------- TMA producer ----------------
+    // ---------------- TMA producer (both CTAs) ----------------
     if (lane == 0) {
       prefetch_tensormap(&p.map_a);
       prefetch_tensormap(&p.map_b);
       unsigned k = 0;
-      for (int tile = blockIdx.x; tile < num_tiles && !aborted(abort_flag); tile += gridDim.x) {
-        const int nt = tile % p.n_tiles, mt = tile / p.n_tiles;
-        const int row0 = mt * p.out_rows - H;  // first GEMM row (halo); may be negative: zero fill
-        const int col0 = nt * kBN;
+      for (int tile = pair; tile < num_tiles && !aborted(abort_flag); tile += npairs) {
+        const int nt = tile % p.n_tiles, mp = tile / p.n_tiles;
+        const int row0 = (2 * mp + (int)crank) * p.out_rows - H;  // this CTA's first GEMM row (halo)
+        const int brow0 = nt * kBN + (int)crank * (kBN / 2);       // this CTA's half of the channel tile
         for (int kb = 0; kb < p.k_blocks; ++kb, ++k) {
           const unsigned s = k % kStages, use = k / kStages;
           if (use > 0 && !mbar_wait(&empty[s], (use - 1) & 1)) {
             *abort_flag = 1;
             break;
           }
-          mbar_arrive_expect_tx(&full[s], kStageBytes);
-          tma_load_2d(smem + kOffA + s * kABytes, &p.map_a, &full[s], kb * kBK, row0);
-          tma_load_2d(smem + kOffB + s * kBBytes, &p.map_b, &full[s], kb * kBK, col0);
+          if (leader) mbar_arrive_expect_tx(&full[s], kPairStageBytes);
+          const uint32_t fb = peer_addr(&full[s], 0);
+          tma_load_2d(smem + kOffA + s * kABytes, &p.map_a, fb, kb * kBK, row0);
+          tma_load_2d(smem + kOffB + s * kBBytes, &p.map_b, fb, kb * kBK, brow0);
         }
       }
-      mbar_drain(full, k, kStages);
+      // The leader waits for the last stages of both CTAs (they complete on
+      // its barriers); the peer's in-flight loads are covered by that wait,
+      // which precedes the cluster barrier both CTAs meet before exiting.
+      if (leader) mbar_drain(full, k, kStages);
     }
   } else if (warp == 1) {
-    // ---------------- MMA issuer ----------------
-    if (lane == 0) {
+    // ---------------- MMA issuer (leader CTA) ----------------
+    if (lane == 0 && leader) {
       unsigned k = 0, j = 0;
       uint64_t* last = nullptr;
       unsigned last_parity = 0;
-      for (int tile = blockIdx.x; tile < num_tiles && !aborted(abort_flag); tile += gridDim.x, ++j) {
+      for (int tile = pair; tile < num_tiles && !aborted(abort_flag); tile += npairs, ++j) {
         const unsigned acc = j & 1, use = j >> 1;
-        // The epilogue must have drained this accumulator (first two tiles: free).
-        if (!mbar_wait(&tempty[acc], (use & 1) ^ 1)) {
+        // Both CTAs' epilogues must have drained this accumulator (first two tiles: free).
+        if (!mbar_wait_cluster(&tempty[acc], (use & 1) ^ 1)) {
           *abort_flag = 1;
           break;
         }
@@ -271,7 +343,9 @@ __global__ void __launch_bounds__(kThreads, 1) inproj_conv_kernel(const __grid_c
           for (int kk = 0; kk < kBK / kUmmaK; ++kk)
             tc_mma(d, sw128_desc(a0 + kk * kUmmaK * 2), sw128_desc(b0 + kk * kUmmaK * 2), kIdesc,
                    (kb | kk) != 0 ? 1u : 0u);
-          tc_commit(&empty[s]);  // the stage is free once these MMAs have read it
+          // Both CTAs' stage s is free once these MMAs have read it.
+          tc_commit(peer_addr(&empty[s], 0));
+          tc_commit(peer_addr(&empty[s], 1));
           last = &empty[s];
           last_parity = u & 1;
         }
@@ -279,34 +353,28 @@ __global__ void __launch_bounds__(kThreads, 1) inproj_conv_kernel(const __grid_c
           *abort_flag = 1;
           break;
         }
-        tc_commit(&tfull[acc]);  // accumulator complete
+        tc_commit(peer_addr(&tfull[acc], 0));  // accumulator complete, in both CTAs
+        tc_commit(peer_addr(&tfull[acc], 1));
       }
-      // Keep the block (and its TMEM) until the MMAs issued last are done.
+      // Keep the pair (and its TMEM) until the MMAs issued last are done.
       if (last != nullptr) (void)mbar_wait(last, last_parity);
     }
   } else {
-    // ---------------- epilogue ----------------
+    // ---------------- epilogue (both CTAs) ----------------
+    const int ew = warp - 2;                // 0..7
     const int q = warp & 3;                 // TMEM lane quarter this warp may access
-    const int r = q * 32 + lane;            // tile row = TMEM lane
-    const int et = threadIdx.x - 64;        // 0..127
+    const int hc = ew >> 2;                 // which 64 channels of a chunk it stages
+    const int r_own = q * 32 + lane;        // tile row this thread stages (= TMEM lane)
+    const int et = threadIdx.x - 64;        // 0..255
+    const int cp = et & 63;                 // channel pair of the chunk this thread walks
+    const int rg = et >> 6;                 // rows it stores: [32 rg, 32 rg + 32)
+    const uint32_t tempty_leader = peer_addr(tempty, 0);
+    typedef Pair<__nv_bfloat16> P;
     unsigned j = 0;
-    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++j) {
-      const int nt = tile % p.n_tiles, mt = tile / p.n_tiles;
+    for (int tile = pair; tile < num_tiles; tile += npairs, ++j) {
+      const int nt = tile % p.n_tiles, mp = tile / p.n_tiles;
       const int col0 = nt * kBN;
-      const i64 m = (i64)mt * p.out_rows - H + r;  // token of this row
-      const bool in_range = m >= 0 && m < p.M;
-      const i64 b = in_range ? m / p.L : 0;
-      const i64 t = in_range ? m - b * p.L : 0;
-      const bool store = r >= H && in_range;
-      // Conv weights and bias of the tile's channels (fp32) into this tile's slot.
-      float* cw = cw_s + (j & 1) * kCwFloats;
-      for (int c = et; c < kBN; c += kEpiWarps * 32) {
-        const i64 n = col0 + c;
-        const bool v = n < p.N;
-#pragma unroll
-        for (int kk = 0; kk < W; ++kk) cw[kk * kBN + c] = v ? __bfloat162float(p.cw[n * p.cw_c + kk * p.cw_k]) : 0.f;
-        cw[(kCwRows - 1) * kBN + c] = (v && p.bias) ? __bfloat162float(p.bias[n * p.bs]) : 0.f;
-      }
+      const i64 mrow0 = (i64)(2 * mp + (int)crank) * p.out_rows - H;  // token of tile row 0
       const unsigned acc = j & 1, use = j >> 1;
       const bool ok = mbar_wait(&tfull[acc], use & 1);
       if (!ok) *abort_flag = 1;
@@ -315,87 +383,124 @@ __global__ void __launch_bounds__(kThreads, 1) inproj_conv_kernel(const __grid_c
       if (epi_bar_or(!ok || aborted(abort_flag))) break;
       tc_fence_after();
       for (int ch = 0; ch < kBN / kChunk; ++ch) {
-        uint32_t v[32];
-        tmem_ld32(tmem_base + ((uint32_t)(q * 32) << 16) + acc * kBN + ch * kChunk, v);
-        tmem_ld_wait();
-        // xBC rounded to bf16, as the unfused GEMM would store it.
-        unsigned char* ybuf = smem + kOffY + (ch & 1) * kYBytes;
-        uint32_t pk[16];
+        // 1. Stage: 64 channels of this thread's row of the chunk, bf16-rounded.
+        uint32_t* yrow = reinterpret_cast<uint32_t*>(smem + kOffY + r_own * kYPitch) + hc * 32;
 #pragma unroll
-        for (int i = 0; i < 16; ++i)
-          pk[i] = Pair<__nv_bfloat16>::pack(f2(__uint_as_float(v[2 * i]), __uint_as_float(v[2 * i + 1])));
-        uint4* yrow = reinterpret_cast<uint4*>(ybuf + r * kYPitch);
+        for (int g = 0; g < 2; ++g) {
+          uint32_t v[32];
+          tmem_ld32(tmem_base + ((uint32_t)(q * 32) << 16) + acc * kBN + ch * kChunk + hc * 64 + g * 32, v);
+          tmem_ld_wait();
+          uint32_t pk[16];
 #pragma unroll
-        for (int i = 0; i < 4; ++i) yrow[i] = make_uint4(pk[4 * i], pk[4 * i + 1], pk[4 * i + 2], pk[4 * i + 3]);
+          for (int i = 0; i < 16; ++i) pk[i] = P::pack(f2(__uint_as_float(v[2 * i]), __uint_as_float(v[2 * i + 1])));
+#pragma unroll
+          for (int i = 0; i < 4; ++i)
+            reinterpret_cast<uint4*>(yrow + g * 16)[i] = make_uint4(pk[4 * i], pk[4 * i + 1], pk[4 * i + 2], pk[4 * i + 3]);
+        }
+        if (ch == kBN / kChunk - 1) {
+          // Accumulator fully read: hand it back to the leader's MMA issuer.
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive_cluster(tempty_leader + acc * 8);
+        }
         epi_bar();
-        const i64 n0 = col0 + ch * kChunk;
-        if (store && n0 < p.N) {
-          // Taps: rows r-H .. r of this chunk (row r-H+kk holds token t-H+kk).
-          float acc_v[32];
+        // 2. Walk: channels (n, n+1); rows [32 rg - 8, 32 rg + 32) of the
+        //    tile, the first 8 (rg > 0) only filling the W-1 window.
+        const i64 n = col0 + ch * kChunk + 2 * cp;
+        if (n < p.N) {
+          float2 wv[W];
 #pragma unroll
-          for (int c = 0; c < 32; ++c) acc_v[c] = cw[(kCwRows - 1) * kBN + ch * kChunk + c];
+          for (int kk = 0; kk < W; ++kk)
+            wv[kk] = f2(__bfloat162float(p.cw[n * p.cw_c + kk * p.cw_k]),
+                        __bfloat162float(p.cw[(n + 1) * p.cw_c + kk * p.cw_k]));
+          const float2 bv = p.bias ? f2(__bfloat162float(p.bias[n * p.bs]), __bfloat162float(p.bias[(n + 1) * p.bs]))
+                                   : f2(0.f, 0.f);
+          const int r0 = rg == 0 ? 0 : 32 * rg - 8;   // first row walked
+          const int rs = rg == 0 ? H : 32 * rg;        // first row stored
+          i64 m = mrow0 + r0;
+          // Sequence position of the first walked row (one division per walk);
+          // rows before token 0 (the first tile's halo) count up to t = 0.
+          i64 b = m >= 0 ? m / p.L : 0;
+          i64 t = m >= 0 ? m - b * p.L : m;
+          float2 xw[H];
 #pragma unroll
-          for (int kk = 0; kk < W; ++kk) {
-            float x[32];
-            const i64 tt = t - H + kk;
-            if (tt >= 0) {
-              const uint4* src = reinterpret_cast<const uint4*>(ybuf + (r - H + kk) * kYPitch);
+          for (int jj = 0; jj < H; ++jj) xw[jj] = f2(0.f, 0.f);
+          const uint32_t* ycol = reinterpret_cast<const uint32_t*>(smem + kOffY) + cp;
+          for (int r = r0; r < 32 * rg + 32; r += 8, m += 8) {
+            uint32_t wd[8];
 #pragma unroll
-              for (int i = 0; i < 4; ++i) {
-                const uint4 u = src[i];
-                const uint32_t w4[4] = {u.x, u.y, u.z, u.w};
+            for (int i = 0; i < 8; ++i) wd[i] = ycol[(r + i) * (kYPitch / 4)];
+            // Clean block: 8 rows of one sequence, none its first token, none
+            // among its last W-1 (final_states), all in range and stored.
+            const bool clean = r >= rs && m >= 0 && m + 8 <= p.M && t >= 1 && t + 8 <= p.L - H;
+            if (clean) {
+              uint32_t o[8];
 #pragma unroll
-                for (int e = 0; e < 4; ++e) {
-                  const float2 f = Pair<__nv_bfloat16>::unpack(w4[e]);
-                  x[8 * i + 2 * e] = f.x;
-                  x[8 * i + 2 * e + 1] = f.y;
-                }
+              for (int i = 0; i < 8; ++i) {
+                const float2 xv = P::unpack(wd[i]);
+                float2 a2 = bv;
+#pragma unroll
+                for (int jj = 0; jj < H; ++jj) a2 = fma2(wv[jj], xw[jj], a2);
+                a2 = fma2(wv[H], xv, a2);
+                if (SILU) a2 = silu2(a2);
+                o[i] = P::pack(a2);
+#pragma unroll
+                for (int jj = 0; jj < H - 1; ++jj) xw[jj] = xw[jj + 1];
+                xw[H - 1] = xv;
               }
+              __nv_bfloat16* dst = p.out + m * p.os_m + n;
+#pragma unroll
+              for (int i = 0; i < 8; ++i) *reinterpret_cast<uint32_t*>(dst + i * p.os_m) = o[i];
+              t += 8;
             } else {
-              // Before the sequence start: initial_states[b, n, t + kk] or 0.
 #pragma unroll
-              for (int c = 0; c < 32; ++c)
-                x[c] = p.init ? __bfloat162float(p.init[b * p.is_b + (n0 + c) * p.is_c + (t + kk) * p.is_l]) : 0.f;
-            }
+              for (int i = 0; i < 8; ++i, ++t) {
+                const i64 mi = m + i;
+                if (t == p.L) {  // next sequence
+                  t = 0;
+                  ++b;
+                }
+                if (mi >= 0 && t == 0) {
+                  // Sequence start: the window is initial_states[b] (or zeros).
 #pragma unroll
-            for (int c = 0; c < 32; ++c) acc_v[c] = fmaf(cw[kk * kBN + ch * kChunk + c], x[c], acc_v[c]);
-          }
-          uint32_t o[16];
+                  for (int jj = 0; jj < H; ++jj)
+                    xw[jj] = p.init ? f2(__bfloat162float(p.init[b * p.is_b + n * p.is_c + jj * p.is_l]),
+                                         __bfloat162float(p.init[b * p.is_b + (n + 1) * p.is_c + jj * p.is_l]))
+                                    : f2(0.f, 0.f);
+                }
+                const float2 xv = P::unpack(wd[i]);
+                if (r + i >= rs && mi >= 0 && mi < p.M) {
+                  float2 a2 = bv;
 #pragma unroll
-          for (int i = 0; i < 16; ++i) {
-            float a0 = acc_v[2 * i], a1 = acc_v[2 * i + 1];
-            if (SILU) {
-              a0 = silu_f(a0);
-              a1 = silu_f(a1);
-            }
-            o[i] = Pair<__nv_bfloat16>::pack(f2(a0, a1));
-          }
-          uint4* dst = reinterpret_cast<uint4*>(p.out + m * p.os_m + n0);
+                  for (int jj = 0; jj < H; ++jj) a2 = fma2(wv[jj], xw[jj], a2);
+                  a2 = fma2(wv[H], xv, a2);
+                  if (SILU) a2 = silu2(a2);
+                  *reinterpret_cast<uint32_t*>(p.out + mi * p.os_m + n) = P::pack(a2);
+                  // final_states: xBC of the last W-1 tokens of the sequence.
+                  if (p.fin && t >= p.L - H) {
+                    __nv_bfloat16* f = p.fin + b * p.fs_b + n * p.fs_c + (t - (p.L - H)) * p.fs_l;
+                    f[0] = __ushort_as_bfloat16((unsigned short)(wd[i] & 0xffffu));
+                    f[p.fs_c] = __ushort_as_bfloat16((unsigned short)(wd[i] >> 16));
+                  }
+                }
 #pragma unroll
-          for (int i = 0; i < 4; ++i) dst[i] = make_uint4(o[4 * i], o[4 * i + 1], o[4 * i + 2], o[4 * i + 3]);
-          // final_states: xBC of the last W-1 tokens of the sequence.
-          if (p.fin && t >= p.L - H) {
-            __nv_bfloat16* f = p.fin + b * p.fs_b + n0 * p.fs_c + (t - (p.L - H)) * p.fs_l;
-#pragma unroll
-            for (int i = 0; i < 16; ++i) {
-              f[(2 * i) * p.fs_c] = __ushort_as_bfloat16((unsigned short)(pk[i] & 0xffffu));
-              f[(2 * i + 1) * p.fs_c] = __ushort_as_bfloat16((unsigned short)(pk[i] >> 16));
+                for (int jj = 0; jj < H - 1; ++jj) xw[jj] = xw[jj + 1];
+                xw[H - 1] = xv;
+              }
             }
           }
         }
+        epi_bar();  // the staging tile is free for the next chunk
       }
-      // Accumulator drained: hand it back to the MMA issuer.
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&tempty[acc]);
     }
   }
 
-  // Teardown: every role has stopped (lanes 1..31 of the producer and MMA
-  // warps wait here for their lane 0); release the TMEM.
+  // Teardown: every role of both CTAs has stopped (lanes 1..31 of the
+  // producer and MMA warps wait here for their lane 0); then both CTAs'
+  // warp 1 release the pair's TMEM.
   __syncwarp();
   tc_fence_before();
-  __syncthreads();
+  cluster_sync();
   if (threadIdx.x == 0 && *abort_flag && p.abort_count) atomicAdd(p.abort_count, 1u);
   if (warp == 1) {
     tc_fence_after();
@@ -448,7 +553,7 @@ cudaError_t launch_fused(const FusedParams& prm, int grid, cudaStream_t stream) 
     if (e != cudaSuccess) return e;
     attr_done.fetch_or(bit, std::memory_order_acq_rel);
   }
-  inproj_conv_kernel<W, SILU><<<grid, kThreads, kSmemBytes, stream>>>(prm);
+  inproj_conv_kernel<W, SILU><<<grid, kThreads, kSmemBytes, stream>>>(prm);  // cluster dims (2, 1, 1)
   return cudaGetLastError();
 }
 
@@ -507,7 +612,7 @@ extern "C" int cc1d_inproj_conv_fwd(const cc1d_inproj_conv_params* q, void* stre
   FusedParams prm;
   std::memset(&prm, 0, sizeof(prm));
   if (!make_kmajor_map(&prm.map_a, q->hidden, M, K, q->hidden_row_stride, kBM) ||
-      !make_kmajor_map(&prm.map_b, q->in_weight, N, K, q->in_weight_row_stride, kBN))
+      !make_kmajor_map(&prm.map_b, q->in_weight, N, K, q->in_weight_row_stride, kBN / 2))
     return report_cuda_error(cudaErrorInvalidValue, "cc1d_inproj_conv_fwd: tensor map");
   prm.cw = static_cast<const __nv_bfloat16*>(q->conv_weight);
   prm.cw_c = q->conv_weight_dim_stride;
@@ -531,7 +636,7 @@ extern "C" int cc1d_inproj_conv_fwd(const cc1d_inproj_conv_params* q, void* stre
   prm.K = K;
   prm.silu = q->silu ? 1 : 0;
   prm.out_rows = kBM - (q->width - 1);
-  prm.m_tiles = (int)ceil_div(M, (i64)prm.out_rows);
+  prm.m_tiles = (int)ceil_div(ceil_div(M, (i64)prm.out_rows), (i64)2);  // pairs of 128-row M tiles
   prm.n_tiles = (int)ceil_div(N, (i64)kBN);
   prm.k_blocks = (int)ceil_div(K, (i64)kBK);
   cudaError_t e = cudaGetSymbolAddress(reinterpret_cast<void**>(&prm.abort_count), g_fused_aborts);
@@ -540,7 +645,7 @@ extern "C" int cc1d_inproj_conv_fwd(const cc1d_inproj_conv_params* q, void* stre
   e = device_info(&dev);
   if (e != cudaSuccess) return report_cuda_error(e, "cc1d_inproj_conv_fwd: device attributes");
   const i64 tiles = (i64)prm.m_tiles * prm.n_tiles;
-  const int grid = (int)std::min<i64>(tiles, dev.sms);
+  const int grid = 2 * (int)std::min<i64>(tiles, dev.sms / 2);  // CTA pairs
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const bool silu = q->silu != 0;
   switch (q->width) {
