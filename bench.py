@@ -650,6 +650,48 @@ def decode_sweep(w, b, rn, peak):
     return out
 
 
+def peak_tflops():
+    p = REPO / "MEASURED_PEAKS.json"
+    if p.is_file():
+        return float(json.loads(p.read_text())["bf16_tflops"]), "measured"
+    return 1590.0, "fallback"
+
+
+def time_fused(peak_tf):
+    """The in_proj GEMM with the conv as its epilogue (one kernel) vs cuBLAS
+    GEMM + the conv kernel, C2 (Mamba-2 2.7B) shapes, W = 4, bias, SiLU,
+    initial and final states.  Tensor-bound: TFLOP/s of the GEMM (2 M N K)."""
+    from causal_conv1d_b200 import _ops
+
+    peak, kind = peak_tf
+    Bf, Lf, Kf, Nf = B, L, 2560, D
+    g = torch.Generator(device="cuda").manual_seed(11)
+    hidden = torch.randn(Bf, Lf, Kf, generator=g, device="cuda").to(DT)
+    win = (torch.randn(Nf, Kf, generator=g, device="cuda") / Kf ** 0.5).to(DT)
+    cw = (torch.rand(Nf, W, generator=g, device="cuda") - 0.5).to(DT)
+    cb = (torch.rand(Nf, generator=g, device="cuda") - 0.5).to(DT)
+    st = torch.randn(Bf, Nf, W - 1, generator=g, device="cuda").to(DT)
+    out = torch.empty(Bf, Lf, Nf, dtype=DT, device="cuda")
+    fs = torch.empty(Bf, Nf, W - 1, dtype=DT, device="cuda")
+    y = torch.empty(Bf, Lf, Nf, dtype=DT, device="cuda")
+    out2 = torch.empty_like(out)
+    fused_ms = _kernel_ms(lambda i: _ops.inproj_conv(hidden, win, cw, cb, st, out, True, fs), 80, 1)
+    gemm_ms = _kernel_ms(lambda i: torch.matmul(hidden, win.t(), out=y), 80, 1)
+
+    def pair(i):
+        torch.matmul(hidden, win.t(), out=y)
+        _ops.fwd(y.transpose(1, 2), cw, cb, None, st, out2.transpose(1, 2), True, fs)
+
+    pair_ms = _kernel_ms(pair, 80, 1)
+    flops = 2 * Bf * Lf * Kf * Nf
+    return {"ms": fused_ms, "tflops": flops / fused_ms / 1e9, "frac": flops / fused_ms / 1e9 / peak,
+            "bound": "tensor", "peak_tflops": peak, "peak_source": f"{kind} bf16 GEMM",
+            "unfused_ms": pair_ms, "cublas_gemm_ms": gemm_ms, "speedup_vs_unfused": pair_ms / fused_ms,
+            "cublas_gemm_tflops": flops / gemm_ms / 1e9,
+            "note": "hidden (8, 2048, 2560) @ in_weight (5376, 2560)^T, conv W=4 + bias + SiLU + states in the "
+                    "epilogue (xBC never stored); unfused = torch.matmul (cuBLAS) + cc1d_fwd"}
+
+
 def time_kernels(peak):
     """Secondary kernels of the metric, each timed alone."""
     from causal_conv1d_b200 import _ops
@@ -770,6 +812,13 @@ def time_kernels(peak):
     res["varlen_states_c4"] = dict(ms=ms, gbs=nb / ms / 1e6, frac=nb / ms / 1e6 / peak, algorithmic_bytes=nb,
                                    note="32 sequences, state_len 3, dim 4096 fp16; launch-latency bound")
     del x, dout, out, dx
+    torch.cuda.empty_cache()
+
+    # Fused neighbour (next row of the path): the in_proj GEMM of the C2
+    # block, xBC = hidden (16384 x 2560) @ in_weight^T (2560 x 5376), with the
+    # conv as its epilogue, against the pair it replaces timed alongside:
+    # cuBLAS GEMM (torch.matmul, xBC stored in bf16), then the conv kernel.
+    res["inproj_conv_fused_c2"] = time_fused(peak_tflops())
     torch.cuda.empty_cache()
 
     # C2 shape with an odd length in the contiguous layout: row pitch

@@ -26,25 +26,31 @@
 //               (M=256, N=256, K=16, bf16 in, fp32 accumulate) and commits
 //               each stage back to both CTAs' producers and, after the last
 //               K step, the accumulator to both CTAs' epilogues.
-//   warps 2..9  epilogue, per 128-channel chunk of the accumulator: each
-//               thread reads half of its TMEM lane (= tile row) with
-//               tcgen05.ld, rounds it to bf16 exactly as the unfused GEMM
-//               would store xBC, and writes it to a shared-memory staging
-//               tile; then the roles turn: a thread owns two adjacent
-//               channels and a quarter of the rows, keeps their weights,
-//               bias and W-1 previous inputs in registers and walks the rows
-//               8 at a time (loads first, then 8 independent outputs) with
-//               packed fp32 math (the tap order and SiLU of every other
-//               kernel of this library), each warp storing 128 contiguous
-//               output bytes per row.
+//   warps 2..9  epilogue: each thread reads half of its TMEM lane (= tile
+//               row) with tcgen05.ld, rounds it to bf16 exactly as the
+//               unfused GEMM would store xBC, and writes it to a 64 KB
+//               shared-memory staging tile -- the accumulator goes back to
+//               the MMA issuer right then; then the roles turn: a thread
+//               owns two adjacent channels and half of the rows, keeps their
+//               weights, bias and W-1 previous inputs in registers and walks
+//               the rows 8 at a time (loads first, then 8 independent
+//               outputs) with packed fp32 math (the tap order and SiLU of
+//               every other kernel of this library), each warp storing 128
+//               contiguous output bytes per row, while the next tiles' MMAs
+//               run.
 // The two accumulators alternate, so the epilogue of one tile overlaps the
 // MMAs of the next.  Per K step a CTA moves 32 KB (its A rows and half of
 // B) for 128 x 256 x 64 MACs: a 128 x 256 tile on one SM moves 48 KB for
 // the same work, and a 256 x 256 tile on one SM needs all of its TMEM for
-// one tile (no overlap).  Measured at the Mamba-2 shape, in order: 485 us
-// (128 x 256, one SM: tensor pipe 32% busy, waiting on TMA), 461 us (256 x
-// 256, one SM), and this design.
-//
+// one tile (no overlap).  Measured on B200 at the Mamba-2 prefill shape
+// (16384 x 2560 @ 2560 x 5376, W = 4), in the order tried: 485 us (one SM,
+// 128 x 256: tensor pipe 32% busy, waiting on TMA), 461 us (one SM,
+// 256 x 256), 433 us (this pairing, row-per-thread epilogue), ~350 us
+// (channel-pair walk, whole accumulator staged before the walk).  Without
+// the conv walk the same kernel runs the GEMM in ~308 us, as fast as cuBLAS
+// (~300-305 us); the walk alone takes ~6.7 us per tile, less than a tile's
+// MMAs (~16 us), so its remaining cost is contention, not serialisation.
+
 // Halo: the conv of output row m needs xBC rows m-(W-1) .. m.  A CTA's 128
 // GEMM rows start W-1 rows before its first output row, so each carries its
 // own halo and produces 128-(W-1) output rows (2.4% extra MMA work at
@@ -71,15 +77,18 @@ namespace {
 constexpr int kBM = 128;       // GEMM rows per tile (tokens, halo included)
 constexpr int kBN = 256;       // channels per tile
 constexpr int kBK = 64;        // K per stage: 64 bf16 = one 128-byte swizzle row
-constexpr int kStages = 5;
+#ifndef CC1D_INPROJ_STAGES
+#define CC1D_INPROJ_STAGES 4
+#endif
+constexpr int kStages = CC1D_INPROJ_STAGES;
 constexpr int kUmmaK = 16;     // K per tcgen05.mma (kind::f16)
-constexpr int kChunk = 128;    // accumulator columns per epilogue step
+constexpr int kChunk = kBN;    // the whole accumulator row is staged at once
 constexpr int kEpiWarps = 8;
 constexpr int kThreads = (2 + kEpiWarps) * 32;
 constexpr unsigned kABytes = kBM * kBK * 2;     // 16 KB
 constexpr unsigned kBBytes = (kBN / 2) * kBK * 2;  // 16 KB: this CTA's half of B
 constexpr unsigned kStageBytes = kABytes + kBBytes;
-constexpr int kYPitch = kChunk * 2 + 16;        // bytes per staged row (padded: conflict-free 16-byte access)
+constexpr int kYPitch = kChunk * 2;             // bytes per staged row; 16-byte units XOR-swizzled by row
 constexpr unsigned kYBytes = kBM * kYPitch;     // the staged chunk (bf16)
 constexpr int kTmemCols = 2 * kBN;              // two accumulators (in each CTA of the pair)
 
@@ -363,11 +372,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     // ---------------- epilogue (both CTAs) ----------------
     const int ew = warp - 2;                // 0..7
     const int q = warp & 3;                 // TMEM lane quarter this warp may access
-    const int hc = ew >> 2;                 // which 64 channels of a chunk it stages
+    const int hc = ew >> 2;                 // which 128 channels of the tile it stages
     const int r_own = q * 32 + lane;        // tile row this thread stages (= TMEM lane)
     const int et = threadIdx.x - 64;        // 0..255
-    const int cp = et & 63;                 // channel pair of the chunk this thread walks
-    const int rg = et >> 6;                 // rows it stores: [32 rg, 32 rg + 32)
+    const int cp = et & 127;                // channel pair of the tile this thread walks
+    const int rg = et >> 7;                 // rows it stores: [64 rg, 64 rg + 64)
     const uint32_t tempty_leader = peer_addr(tempty, 0);
     typedef Pair<__nv_bfloat16> P;
     unsigned j = 0;
@@ -375,6 +384,18 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       const int nt = tile % p.n_tiles, mp = tile / p.n_tiles;
       const int col0 = nt * kBN;
       const i64 mrow0 = (i64)(2 * mp + (int)crank) * p.out_rows - H;  // token of tile row 0
+      // Conv weights and bias of this thread's channel pair, fetched before
+      // waiting for the accumulator so that their latency overlaps the MMAs.
+      const i64 n = col0 + 2 * cp;
+      const bool nv = n < p.N;
+      float2 wv[W];
+#pragma unroll
+      for (int kk = 0; kk < W; ++kk)
+        wv[kk] = nv ? f2(__bfloat162float(p.cw[n * p.cw_c + kk * p.cw_k]),
+                         __bfloat162float(p.cw[(n + 1) * p.cw_c + kk * p.cw_k]))
+                    : f2(0.f, 0.f);
+      const float2 bv = (nv && p.bias) ? f2(__bfloat162float(p.bias[n * p.bs]), __bfloat162float(p.bias[(n + 1) * p.bs]))
+                                       : f2(0.f, 0.f);
       const unsigned acc = j & 1, use = j >> 1;
       const bool ok = mbar_wait(&tfull[acc], use & 1);
       if (!ok) *abort_flag = 1;
@@ -382,115 +403,112 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       // matching): stop if any of them timed out or another role aborted.
       if (epi_bar_or(!ok || aborted(abort_flag))) break;
       tc_fence_after();
-      for (int ch = 0; ch < kBN / kChunk; ++ch) {
-        // 1. Stage: 64 channels of this thread's row of the chunk, bf16-rounded.
-        uint32_t* yrow = reinterpret_cast<uint32_t*>(smem + kOffY + r_own * kYPitch) + hc * 32;
+      // 1. Stage: 128 channels of this thread's row, bf16-rounded.  16-byte
+      //    unit u of row r sits at unit u ^ (r & 7): rows 128 bytes apart hit
+      //    the same banks, so the XOR spreads both the row-wise stores (8
+      //    rows per phase) and the column-wise loads of the walk.
+      {
+        uint4* yrow = reinterpret_cast<uint4*>(smem + kOffY + r_own * kYPitch);
 #pragma unroll
-        for (int g = 0; g < 2; ++g) {
+        for (int g = 0; g < 4; ++g) {
           uint32_t v[32];
-          tmem_ld32(tmem_base + ((uint32_t)(q * 32) << 16) + acc * kBN + ch * kChunk + hc * 64 + g * 32, v);
+          tmem_ld32(tmem_base + ((uint32_t)(q * 32) << 16) + acc * kBN + hc * 128 + g * 32, v);
           tmem_ld_wait();
           uint32_t pk[16];
 #pragma unroll
           for (int i = 0; i < 16; ++i) pk[i] = P::pack(f2(__uint_as_float(v[2 * i]), __uint_as_float(v[2 * i + 1])));
 #pragma unroll
-          for (int i = 0; i < 4; ++i)
-            reinterpret_cast<uint4*>(yrow + g * 16)[i] = make_uint4(pk[4 * i], pk[4 * i + 1], pk[4 * i + 2], pk[4 * i + 3]);
+          for (int i = 0; i < 4; ++i) {
+            const int u = hc * 16 + g * 4 + i;  // 16-byte unit (8 channels) of the row
+            yrow[u ^ (r_own & 7)] = make_uint4(pk[4 * i], pk[4 * i + 1], pk[4 * i + 2], pk[4 * i + 3]);
+          }
         }
-        if (ch == kBN / kChunk - 1) {
-          // Accumulator fully read: hand it back to the leader's MMA issuer.
-          tc_fence_before();
-          __syncwarp();
-          if (lane == 0) mbar_arrive_cluster(tempty_leader + acc * 8);
-        }
-        epi_bar();
-        // 2. Walk: channels (n, n+1); rows [32 rg - 8, 32 rg + 32) of the
-        //    tile, the first 8 (rg > 0) only filling the W-1 window.
-        const i64 n = col0 + ch * kChunk + 2 * cp;
-        if (n < p.N) {
-          float2 wv[W];
+        // Accumulator fully read: hand it back to the leader's MMA issuer.
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive_cluster(tempty_leader + acc * 8);
+      }
+      epi_bar();
+      // 2. Walk: channels (n, n+1); rows [64 rg - 8, 64 rg + 64) of the tile,
+      //    the first 8 (rg > 0) only filling the W-1 window.  The next
+      //    tile's staging waits at its opening barrier for every walk to end.
+      if (nv) {
+        const int r0 = rg == 0 ? 0 : 64 * rg - 8;   // first row walked
+        const int rs = rg == 0 ? H : 64 * rg;        // first row stored
+        i64 m = mrow0 + r0;
+        // Sequence position of the first walked row (one division per walk);
+        // rows before token 0 (the first tile's halo) count up to t = 0.
+        i64 b = m >= 0 ? m / p.L : 0;
+        i64 t = m >= 0 ? m - b * p.L : m;
+        float2 xw[H];
 #pragma unroll
-          for (int kk = 0; kk < W; ++kk)
-            wv[kk] = f2(__bfloat162float(p.cw[n * p.cw_c + kk * p.cw_k]),
-                        __bfloat162float(p.cw[(n + 1) * p.cw_c + kk * p.cw_k]));
-          const float2 bv = p.bias ? f2(__bfloat162float(p.bias[n * p.bs]), __bfloat162float(p.bias[(n + 1) * p.bs]))
-                                   : f2(0.f, 0.f);
-          const int r0 = rg == 0 ? 0 : 32 * rg - 8;   // first row walked
-          const int rs = rg == 0 ? H : 32 * rg;        // first row stored
-          i64 m = mrow0 + r0;
-          // Sequence position of the first walked row (one division per walk);
-          // rows before token 0 (the first tile's halo) count up to t = 0.
-          i64 b = m >= 0 ? m / p.L : 0;
-          i64 t = m >= 0 ? m - b * p.L : m;
-          float2 xw[H];
+        for (int jj = 0; jj < H; ++jj) xw[jj] = f2(0.f, 0.f);
+        const uint32_t* ybase = reinterpret_cast<const uint32_t*>(smem + kOffY);
+        const int cu = cp >> 2, cw4 = cp & 3;  // 16-byte unit and word of this channel pair
+        for (int r = r0; r < 64 * rg + 64; r += 8, m += 8) {
+          uint32_t wd[8];
 #pragma unroll
-          for (int jj = 0; jj < H; ++jj) xw[jj] = f2(0.f, 0.f);
-          const uint32_t* ycol = reinterpret_cast<const uint32_t*>(smem + kOffY) + cp;
-          for (int r = r0; r < 32 * rg + 32; r += 8, m += 8) {
-            uint32_t wd[8];
+          for (int i = 0; i < 8; ++i)  // r is a multiple of 8: row r + i has (r + i) & 7 == i
+            wd[i] = ybase[(r + i) * (kYPitch / 4) + ((cu ^ i) << 2) + cw4];
+          // Clean block: 8 rows of one sequence, none its first token, none
+          // among its last W-1 (final_states), all in range and stored.
+          const bool clean = r >= rs && m >= 0 && m + 8 <= p.M && t >= 1 && t + 8 <= p.L - H;
+          if (clean) {
+            uint32_t o[8];
 #pragma unroll
-            for (int i = 0; i < 8; ++i) wd[i] = ycol[(r + i) * (kYPitch / 4)];
-            // Clean block: 8 rows of one sequence, none its first token, none
-            // among its last W-1 (final_states), all in range and stored.
-            const bool clean = r >= rs && m >= 0 && m + 8 <= p.M && t >= 1 && t + 8 <= p.L - H;
-            if (clean) {
-              uint32_t o[8];
+            for (int i = 0; i < 8; ++i) {
+              const float2 xv = P::unpack(wd[i]);
+              float2 a2 = bv;
 #pragma unroll
-              for (int i = 0; i < 8; ++i) {
-                const float2 xv = P::unpack(wd[i]);
+              for (int jj = 0; jj < H; ++jj) a2 = fma2(wv[jj], xw[jj], a2);
+              a2 = fma2(wv[H], xv, a2);
+              if (SILU) a2 = silu2(a2);
+              o[i] = P::pack(a2);
+#pragma unroll
+              for (int jj = 0; jj < H - 1; ++jj) xw[jj] = xw[jj + 1];
+              xw[H - 1] = xv;
+            }
+            __nv_bfloat16* dst = p.out + m * p.os_m + n;
+#pragma unroll
+            for (int i = 0; i < 8; ++i) *reinterpret_cast<uint32_t*>(dst + i * p.os_m) = o[i];
+            t += 8;
+          } else {
+#pragma unroll
+            for (int i = 0; i < 8; ++i, ++t) {
+              const i64 mi = m + i;
+              if (t == p.L) {  // next sequence
+                t = 0;
+                ++b;
+              }
+              if (mi >= 0 && t == 0) {
+                // Sequence start: the window is initial_states[b] (or zeros).
+#pragma unroll
+                for (int jj = 0; jj < H; ++jj)
+                  xw[jj] = p.init ? f2(__bfloat162float(p.init[b * p.is_b + n * p.is_c + jj * p.is_l]),
+                                       __bfloat162float(p.init[b * p.is_b + (n + 1) * p.is_c + jj * p.is_l]))
+                                  : f2(0.f, 0.f);
+              }
+              const float2 xv = P::unpack(wd[i]);
+              if (r + i >= rs && mi >= 0 && mi < p.M) {
                 float2 a2 = bv;
 #pragma unroll
                 for (int jj = 0; jj < H; ++jj) a2 = fma2(wv[jj], xw[jj], a2);
                 a2 = fma2(wv[H], xv, a2);
                 if (SILU) a2 = silu2(a2);
-                o[i] = P::pack(a2);
-#pragma unroll
-                for (int jj = 0; jj < H - 1; ++jj) xw[jj] = xw[jj + 1];
-                xw[H - 1] = xv;
+                *reinterpret_cast<uint32_t*>(p.out + mi * p.os_m + n) = P::pack(a2);
+                // final_states: xBC of the last W-1 tokens of the sequence.
+                if (p.fin && t >= p.L - H) {
+                  __nv_bfloat16* f = p.fin + b * p.fs_b + n * p.fs_c + (t - (p.L - H)) * p.fs_l;
+                  f[0] = __ushort_as_bfloat16((unsigned short)(wd[i] & 0xffffu));
+                  f[p.fs_c] = __ushort_as_bfloat16((unsigned short)(wd[i] >> 16));
+                }
               }
-              __nv_bfloat16* dst = p.out + m * p.os_m + n;
 #pragma unroll
-              for (int i = 0; i < 8; ++i) *reinterpret_cast<uint32_t*>(dst + i * p.os_m) = o[i];
-              t += 8;
-            } else {
-#pragma unroll
-              for (int i = 0; i < 8; ++i, ++t) {
-                const i64 mi = m + i;
-                if (t == p.L) {  // next sequence
-                  t = 0;
-                  ++b;
-                }
-                if (mi >= 0 && t == 0) {
-                  // Sequence start: the window is initial_states[b] (or zeros).
-#pragma unroll
-                  for (int jj = 0; jj < H; ++jj)
-                    xw[jj] = p.init ? f2(__bfloat162float(p.init[b * p.is_b + n * p.is_c + jj * p.is_l]),
-                                         __bfloat162float(p.init[b * p.is_b + (n + 1) * p.is_c + jj * p.is_l]))
-                                    : f2(0.f, 0.f);
-                }
-                const float2 xv = P::unpack(wd[i]);
-                if (r + i >= rs && mi >= 0 && mi < p.M) {
-                  float2 a2 = bv;
-#pragma unroll
-                  for (int jj = 0; jj < H; ++jj) a2 = fma2(wv[jj], xw[jj], a2);
-                  a2 = fma2(wv[H], xv, a2);
-                  if (SILU) a2 = silu2(a2);
-                  *reinterpret_cast<uint32_t*>(p.out + mi * p.os_m + n) = P::pack(a2);
-                  // final_states: xBC of the last W-1 tokens of the sequence.
-                  if (p.fin && t >= p.L - H) {
-                    __nv_bfloat16* f = p.fin + b * p.fs_b + n * p.fs_c + (t - (p.L - H)) * p.fs_l;
-                    f[0] = __ushort_as_bfloat16((unsigned short)(wd[i] & 0xffffu));
-                    f[p.fs_c] = __ushort_as_bfloat16((unsigned short)(wd[i] >> 16));
-                  }
-                }
-#pragma unroll
-                for (int jj = 0; jj < H - 1; ++jj) xw[jj] = xw[jj + 1];
-                xw[H - 1] = xv;
-              }
+              for (int jj = 0; jj < H - 1; ++jj) xw[jj] = xw[jj + 1];
+              xw[H - 1] = xv;
             }
           }
         }
-        epi_bar();  // the staging tile is free for the next chunk
       }
     }
   }
