@@ -738,8 +738,9 @@ def time_kernels(peak):
     res["decode_batch_sweep"] = decode_sweep(w, b, rn, peak)
 
     # Next rows of the path: a 4-token decode burst (speculative decoding) on
-    # the C3a pool, and the C3a step with a channel-last conv_state pool
-    # (strides (3*D, 1, D)); both use the generic update kernel.
+    # the C3a pool (update_lin_kernel), and the C3a / C3b steps with the
+    # conv_state stored channel-last (strides (S*D, 1, D), vLLM's layout;
+    # update_vec_kernel's channel-last linear and circular modes).
     Lb = 4
     xs = [rn(Bu, Du, Lb) for _ in range(sets)]
     pools = [rn(512, Du, W - 1) for _ in range(sets)]
@@ -757,8 +758,16 @@ def time_kernels(peak):
     nbytes = Bu * Du * (2 + 2 + 6 + 6) + Du * (W + 1) * 2 + Bu * 4
     res["update_c3a_chanlast_state"] = dict(ms=ms, gbs=nbytes / ms / 1e6, frac=nbytes / ms / 1e6 / peak,
                                             tokens_per_s=Bu / (ms / 1e3), algorithmic_bytes=nbytes,
-                                            note="C3a with conv_state pool stored (512, 3, 5376), generic kernel")
-    del xs, pools, outs
+                                            note="C3a with conv_state pool stored (512, 3, 5376)")
+    del pools
+    states = [rn(Bu, 8, Du).transpose(1, 2) for _ in range(sets)]
+    cache = [torch.randint(0, 1024, (Bu,), device="cuda", dtype=torch.int32) for _ in range(sets)]
+    ms = _kernel_ms(lambda i: _ops.update(xs[i], states[i], w, b, cache[i], None, outs[i], True), 800, sets)
+    nbytes = Bu * Du * (2 + 2 + 6 + 2) + Du * (W + 1) * 2 + Bu * 4
+    res["update_c3b_chanlast_state"] = dict(ms=ms, gbs=nbytes / ms / 1e6, frac=nbytes / ms / 1e6 / peak,
+                                            tokens_per_s=Bu / (ms / 1e3), algorithmic_bytes=nbytes,
+                                            note="C3b with the circular state stored (256, 8, 5376)")
+    del xs, states, outs
     torch.cuda.empty_cache()
 
     # C4: varlen packed prefill fp16 (1, 4096, 65536) channel-last + seq_idx.
@@ -996,7 +1005,7 @@ def run_only(args):
         dw, db = torch.empty(Dv, W, dtype=dt, device="cuda"), torch.empty(Dv, dtype=dt, device="cuda")
         fn = (lambda: _ops.fwd(x, wv, bv, seq, None, out, True, None)) if op == "fwd_c4" else \
             (lambda: _ops.bwd(x, wv, bv, dout, seq, None, None, dx, dwdb, None, dw, db, True))
-    elif op in ("update_c3a", "update_c3b", "update_burst4", "update_c3a_chanlast"):
+    elif op in ("update_c3a", "update_c3b", "update_burst4", "update_c3a_chanlast", "update_c3b_chanlast"):
         Bu, Du = 256, 5376
         w, b = ru(Du, W), ru(Du)
         x = rn(Bu, Du, 4 if op == "update_burst4" else 1)
@@ -1010,7 +1019,7 @@ def run_only(args):
             idx = torch.randperm(512, device="cuda")[:Bu].to(torch.int32)
             fn = lambda: _ops.update(x, pool, w, b, None, idx, out, True)  # noqa: E731
         else:
-            state = rn(Bu, Du, 8)
+            state = rn(Bu, Du, 8) if op == "update_c3b" else rn(Bu, 8, Du).transpose(1, 2)
             cache = torch.randint(0, 1024, (Bu,), device="cuda", dtype=torch.int32)
             fn = lambda: _ops.update(x, state, w, b, cache, None, out, True)  # noqa: E731
     else:
@@ -1050,7 +1059,7 @@ def main():
     ap.add_argument("--skip-c5", action="store_true", help="skip the C5 sweep (BASELINE configs[4])")
     ap.add_argument("--only", default=None,
                     help="launch one op alone (fwd_c2, bwd_c2, update_c3a, update_c3b, update_burst4, "
-                         "update_c3a_chanlast, fwd_c4, bwd_c4, fwd_c5, bwd_c5) --reps times, for profilers; "
+                         "update_c3a_chanlast, update_c3b_chanlast, fwd_c4, bwd_c4, fwd_c5, bwd_c5) --reps times, for profilers; "
                          "prints no contract line")
     ap.add_argument("--reps", type=int, default=3)
     ap.add_argument("--c5-batch", type=int, default=64, help="batch of the C5 shape in --only mode")

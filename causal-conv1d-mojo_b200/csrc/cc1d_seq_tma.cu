@@ -12,9 +12,10 @@
 // lane 31 of the current one, so x is read from HBM exactly once.
 //
 // The backward walks the tiles forward too.  dx at a position needs dpre of
-// the next W-1 positions; for lane 31 those live in the next tile, so every
-// tile's dx is emitted one tile late (its dpre kept in registers), with the
-// dpre just past the segment computed from a few scalar loads.
+// the next W-1 positions; its tiles overlap by one lane (they advance 248
+// positions), so lane 31 recomputes the dpre lane 30's dx needs and every
+// tile's dx is emitted within the tile.  (The shifted-row backward instead
+// emits each tile's dx one tile late.)
 // Semantics are those of cc1d_fwd.cu / cc1d_bwd.cu (reference CPU kernels
 // src/causal_conv1d_mojo/fwd_cpu/kernel.mojo:64-117,
 // bwd_full_cpu/kernel.mojo:26-314; final/initial states as
@@ -70,6 +71,7 @@ constexpr int kSW = CC1D_SEQ_WARPS;  // consumer warps
 constexpr int kRows = 2 * kSW;       // channel rows per tile
 constexpr int kTL = 256;             // positions per tile (32 lanes x 8)
 constexpr int kThreadsSeq = (kSW + 1) * 32;
+constexpr int kBwdStep = kTL - 8;    // backward tiles advance by 31 lanes (see bwd_seq_tma_kernel)
 
 template <typename T>
 constexpr unsigned seq_tile_bytes() {
@@ -125,13 +127,14 @@ __device__ __forceinline__ void lds_ids(const unsigned char* ids, int lane, int 
 }
 
 // Halo ids of a lane (positions 8*lane-H .. 8*lane-1): from lane-1, or for
-// lane 0 from the previous tile (carry, updated to this tile's last ids).
+// lane 0 from the previous tile (carry, updated to the last ids of lane
+// `last`, the last lane the next tile does not overlap).
 template <int H>
-__device__ __forceinline__ void ids_halo(const int (&sid)[8], int (&carry)[H], int (&hs)[H], int lane) {
+__device__ __forceinline__ void ids_halo(const int (&sid)[8], int (&carry)[H], int (&hs)[H], int lane, int last = 31) {
 #pragma unroll
   for (int j = 0; j < H; ++j) {
     const int up = __shfl_up_sync(kFull, sid[8 - H + j], 1);
-    const int nc = __shfl_sync(kFull, sid[8 - H + j], 31);
+    const int nc = __shfl_sync(kFull, sid[8 - H + j], last);
     hs[j] = lane == 0 ? carry[j] : up;
     carry[j] = nc;
   }
@@ -376,7 +379,7 @@ __global__ void __launch_bounds__(kThreadsSeq, CC1D_SEQ_FWD_MIN_BLOCKS) fwd_seq_
 // H positions after them (rh), plus dfinal where final_states read them.
 template <typename T, int W>
 __device__ __forceinline__ void emit_dx(const float2 (&d)[8], const float2 (&rh)[W - 1], const float2 (&wp)[W],
-                                        i64 pos, i64 t1, const BwdArgs& a, T* dxa, const T* fa, bool va, bool vb) {
+                                        i64 pos, bool store, const BwdArgs& a, T* dxa, const T* fa, bool va, bool vb) {
   constexpr int H = W - 1;
   float ea[8], eb[8];
 #pragma unroll
@@ -401,7 +404,7 @@ __device__ __forceinline__ void emit_dx(const float2 (&d)[8], const float2 (&rh)
       }
     }
   }
-  if (pos < t1) {
+  if (store) {
     if (va) stg8<T>(dxa + pos, ea);
     if (vb) stg8<T>(dxa + a.dxs_c + pos, eb);
   }
@@ -411,8 +414,8 @@ __device__ __forceinline__ void emit_dx(const float2 (&d)[8], const float2 (&rh)
 // that carry q's sequence id (dpre is already 0 at padding).
 template <typename T, int W>
 __device__ __forceinline__ void emit_dx_seq(const float2 (&d)[8], const float2 (&rh)[W - 1], const int (&sd)[8],
-                                            const int (&srh)[W - 1], const float2 (&wp)[W], i64 pos, i64 t1, T* dxa,
-                                            i64 dxs_c, bool va, bool vb) {
+                                            const int (&srh)[W - 1], const float2 (&wp)[W], i64 pos, bool store,
+                                            T* dxa, i64 dxs_c, bool va, bool vb) {
   constexpr int H = W - 1;
   float ea[8], eb[8];
 #pragma unroll
@@ -427,12 +430,22 @@ __device__ __forceinline__ void emit_dx_seq(const float2 (&d)[8], const float2 (
     ea[i] = acc.x;
     eb[i] = acc.y;
   }
-  if (pos < t1) {
+  if (store) {
     if (va) stg8<T>(dxa + pos, ea);
     if (vb) stg8<T>(dxa + dxs_c + pos, eb);
   }
 }
 
+// The backward's tiles overlap by one lane: a tile holds 256 positions
+// [t, t + 256) but the walk advances kBwdStep = 248, so lanes 0..30 own
+// [t, t + 248) and lane 31 only recomputes dpre of [t + 248, t + 256) -- the
+// right halo of lane 30's dx, owned by the next tile.  Every tile's dx is
+// therefore emitted within the tile (no dpre carried to the next one), and
+// a segment's last tile already holds the dpre just past the segment, where
+// lane 31 (or the lanes past the segment end) compute it from the tile like
+// any other position.  The overlap costs 1/32 of the arithmetic and an
+// 8-position L2 re-read per tile; it frees the registers of a tile of
+// delayed dpre and the scalar loads of the segment's tail.
 template <typename T, int W, bool HAS_SEQ, bool SILU>
 __global__ void __launch_bounds__(kThreadsSeq, W > 5 ? 1 : (HAS_SEQ ? CC1D_SEQ_BWD_IDS_MIN_BLOCKS : CC1D_SEQ_BWD_MIN_BLOCKS)) bwd_seq_tma_kernel(const __grid_constant__ SeqBwdParams p) {
   constexpr int H = W - 1;
@@ -470,7 +483,7 @@ __global__ void __launch_bounds__(kThreadsSeq, W > 5 ? 1 : (HAS_SEQ ? CC1D_SEQ_B
       prefetch_tensormap(&p.map_g);
       if (HAS_SEQ) prefetch_tensormap(&p.map_s);
       unsigned k = 0;
-      for (i64 t = t0; t < t1; t += kTL, ++k) {
+      for (i64 t = t0; t < t1; t += kBwdStep, ++k) {
         const unsigned s = k % NS, use = k / NS;
         if (use > 0 && !mbar_wait(&empty[s], (use - 1) & 1)) break;  // consumers stopped
         mbar_arrive_expect_tx(&full[s], SB);
@@ -493,49 +506,25 @@ __global__ void __launch_bounds__(kThreadsSeq, W > 5 ? 1 : (HAS_SEQ ? CC1D_SEQ_B
     wp[k] = f2(va ? Cvt<T>::f(wt[ra * a.ws_c + k * a.ws_k]) : 0.f, vb ? Cvt<T>::f(wt[(ra + 1) * a.ws_c + k * a.ws_k]) : 0.f);
   const float2 bp = f2((bias && va) ? Cvt<T>::f(bias[ra * a.bs]) : 0.f, (bias && vb) ? Cvt<T>::f(bias[(ra + 1) * a.bs]) : 0.f);
   const T* __restrict__ xr = static_cast<const T*>(a.x) + b * a.xs_b + ra * a.xs_c;
-  const T* __restrict__ gr = static_cast<const T*>(a.dout) + b * a.gs_b + ra * a.gs_c;
   const T* __restrict__ ir = a.init ? static_cast<const T*>(a.init) + b * a.is_b + ra * a.is_c : nullptr;
   const T* __restrict__ fa = a.dfin ? static_cast<const T*>(a.dfin) + b * a.fs_b + ra * a.fs_c : nullptr;
   T* __restrict__ dxa = static_cast<T*>(a.dx) + b * a.dxs_b + ra * a.dxs_c;
 
+  // Halo of lane 0 in the first tile: xc at t0-H .. t0-1 (and its ids).
   float2 carry[H];
 #pragma unroll
   for (int j = 0; j < H; ++j) carry[j] = xc_pair(xr, a.xs_c, a.xs_l, ir, a.is_c, a.is_l, H, t0 - H + j, va, vb);
-  const int* __restrict__ seq = HAS_SEQ ? a.seq + b * a.ss_b : nullptr;
   int scarry[H];
 #pragma unroll
-  for (int j = 0; j < H; ++j) scarry[j] = HAS_SEQ ? seq_at(seq, a.ss_l, t0 - H + j, a.L) : 0;
-  // dpre just past the segment (0 past the sequence), for lane 31's last dx,
-  // and (with seq_idx) the ids of those positions.
-  float2 rend[H];
-  int srend[H];
-#pragma unroll
-  for (int j = 0; j < H; ++j) {
-    const i64 q = t1 + j;
-    rend[j] = f2(0.f, 0.f);
-    srend[j] = HAS_SEQ ? seq_at(seq, a.ss_l, q, a.L) : 0;
-    if (q < a.L && (!HAS_SEQ || srend[j] >= 0)) {
-      float2 pre = bp;
-#pragma unroll
-      for (int kk = 0; kk < W; ++kk) {
-        if (HAS_SEQ && seq_at(seq, a.ss_l, q - H + kk, a.L) != srend[j]) continue;
-        pre = fma2(wp[kk], xc_pair(xr, a.xs_c, a.xs_l, ir, a.is_c, a.is_l, H, q - H + kk, va, vb), pre);
-      }
-      const float2 g = f2(va ? Cvt<T>::f(gr[q * a.gs_l]) : 0.f, vb ? Cvt<T>::f(gr[a.gs_c + q * a.gs_l]) : 0.f);
-      rend[j] = SILU ? mul2(g, silu_grad2(pre)) : g;
-    }
-  }
+  for (int j = 0; j < H; ++j) scarry[j] = HAS_SEQ ? seq_at(a.seq + b * a.ss_b, a.ss_l, t0 - H + j, a.L) : 0;
 
   float2 dw[W];
 #pragma unroll
   for (int k = 0; k < W; ++k) dw[k] = f2(0.f, 0.f);
   float2 db = f2(0.f, 0.f);
-  float2 dprev[8];
-  int sprev[8];
-  i64 tprev = -1;
 
   unsigned k = 0;
-  for (i64 t = t0; t < t1; t += kTL, ++k) {
+  for (i64 t = t0; t < t1; t += kBwdStep, ++k) {
     const unsigned s = k % NS, use = k / NS;
     if (!mbar_wait(&full[s], use & 1)) return;
     float xa[8], xb[8], ga[8], gb[8];
@@ -550,20 +539,23 @@ __global__ void __launch_bounds__(kThreadsSeq, W > 5 ? 1 : (HAS_SEQ ? CC1D_SEQ_B
     float2 xp[8], d[8];
 #pragma unroll
     for (int i = 0; i < 8; ++i) xp[i] = f2(xa[i], xb[i]);
+    // Left halo from lane - 1; lane 0 takes the previous tile's lane 30.
     float2 h[H];
 #pragma unroll
     for (int j = 0; j < H; ++j) {
       const float2 up = shfl_up2(xp[8 - H + j], 1);
-      const float2 nc = shfl2(xp[8 - H + j], 31);
+      const float2 nc = shfl2(xp[8 - H + j], 31 - 1);
       h[j] = lane == 0 ? carry[j] : up;
       carry[j] = nc;
     }
     int hs[H];
     bool gated = false;
     if (HAS_SEQ) {
-      ids_halo<H>(sid, scarry, hs, lane);
+      ids_halo<H>(sid, scarry, hs, lane, 31 - 1);
       gated = !ids_uniform<H>(sid, hs);
     }
+    const i64 pos = t + 8 * lane;
+    const bool own = lane < 31 && pos < t1;  // positions whose dx, dweight and dbias this tile produces
     if (!gated) {
 #pragma unroll
       for (int i = 0; i < 8; ++i) {
@@ -575,11 +567,13 @@ __global__ void __launch_bounds__(kThreadsSeq, W > 5 ? 1 : (HAS_SEQ ? CC1D_SEQ_B
         }
         const float2 g = f2(ga[i], gb[i]);
         d[i] = SILU ? mul2(g, silu_grad2(pre)) : g;
-        db = add2(db, d[i]);
+        if (own) {
+          db = add2(db, d[i]);
 #pragma unroll
-        for (int kk = 0; kk < W; ++kk) {
-          const int q = i - H + kk;
-          dw[kk] = fma2(d[i], q >= 0 ? xp[q >= 0 ? q : 0] : h[q >= 0 ? 0 : q + H], dw[kk]);
+          for (int kk = 0; kk < W; ++kk) {
+            const int q = i - H + kk;
+            dw[kk] = fma2(d[i], q >= 0 ? xp[q >= 0 ? q : 0] : h[q >= 0 ? 0 : q + H], dw[kk]);
+          }
         }
       }
     } else {
@@ -597,41 +591,33 @@ __global__ void __launch_bounds__(kThreadsSeq, W > 5 ? 1 : (HAS_SEQ ? CC1D_SEQ_B
         const float2 g = f2(ga[i], gb[i]);
         d[i] = SILU ? mul2(g, silu_grad2(pre)) : g;
         if (si < 0) d[i] = f2(0.f, 0.f);
-        db = add2(db, d[i]);
+        if (own) {
+          db = add2(db, d[i]);
 #pragma unroll
-        for (int kk = 0; kk < W; ++kk) {
-          const int q = i - H + kk;
-          const int sq = q >= 0 ? sid[q >= 0 ? q : 0] : hs[q >= 0 ? 0 : q + H];
-          if (sq == si) dw[kk] = fma2(d[i], q >= 0 ? xp[q >= 0 ? q : 0] : h[q >= 0 ? 0 : q + H], dw[kk]);
+          for (int kk = 0; kk < W; ++kk) {
+            const int q = i - H + kk;
+            const int sq = q >= 0 ? sid[q >= 0 ? q : 0] : hs[q >= 0 ? 0 : q + H];
+            if (sq == si) dw[kk] = fma2(d[i], q >= 0 ? xp[q >= 0 ? q : 0] : h[q >= 0 ? 0 : q + H], dw[kk]);
+          }
         }
       }
     }
-    // dx of the previous tile: lane 31 now has its right halo (this tile's
-    // first dpre values, from lane 0).
-    if (tprev >= 0) {
-      float2 rh[H];
+    // dx of this tile: the right halo of lane l is lane l + 1's first dpre
+    // (lane 30 reads the overlap lane; lane 31 stores nothing).
+    float2 rh[H];
 #pragma unroll
-      for (int j = 0; j < H; ++j) {
-        const float2 nxt = shfl_down2(dprev[j], 1);
-        const float2 first = shfl2(d[j], 0);
-        rh[j] = lane == 31 ? first : nxt;
-      }
-      bool egated = false;
-      int srh[H];
-      if (HAS_SEQ) {
+    for (int j = 0; j < H; ++j) rh[j] = shfl_down2(d[j], 1);
+    bool egated = false;
+    int srh[H];
+    if (HAS_SEQ) {
 #pragma unroll
-        for (int j = 0; j < H; ++j) {
-          const int nxt = __shfl_down_sync(kFull, sprev[j], 1);
-          const int first = __shfl_sync(kFull, sid[j], 0);
-          srh[j] = lane == 31 ? first : nxt;
-        }
-        egated = !ids_uniform<H>(sprev, srh);
-      }
-      if (egated)
-        emit_dx_seq<T, W>(dprev, rh, sprev, srh, wp, tprev + 8 * lane, t1, dxa, a.dxs_c, va, vb);
-      else
-        emit_dx<T, W>(dprev, rh, wp, tprev + 8 * lane, t1, a, dxa, fa, va, vb);
+      for (int j = 0; j < H; ++j) srh[j] = __shfl_down_sync(kFull, sid[j], 1);
+      egated = !ids_uniform<H>(sid, srh);
     }
+    if (egated)
+      emit_dx_seq<T, W>(d, rh, sid, srh, wp, pos, own, dxa, a.dxs_c, va, vb);
+    else
+      emit_dx<T, W>(d, rh, wp, pos, own, a, dxa, fa, va, vb);
     // dinitial_states: dpre of positions 0 .. H-1 live in lane 0 of tile 0.
     if (t == 0 && lane == 0 && a.dinit != nullptr) {
       T* di = static_cast<T*>(a.dinit) + b * a.dis_b + ra * a.dis_c;
@@ -648,34 +634,6 @@ __global__ void __launch_bounds__(kThreadsSeq, W > 5 ? 1 : (HAS_SEQ ? CC1D_SEQ_B
         if (vb) di[a.dis_c + i * a.dis_l] = Cvt<T>::to(acc.y);
       }
     }
-#pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      dprev[i] = d[i];
-      if (HAS_SEQ) sprev[i] = sid[i];
-    }
-    tprev = t;
-  }
-  if (tprev >= 0) {
-    float2 rh[H];
-#pragma unroll
-    for (int j = 0; j < H; ++j) {
-      const float2 nxt = shfl_down2(dprev[j], 1);
-      rh[j] = lane == 31 ? rend[j] : nxt;
-    }
-    bool egated = false;
-    int srh[H];
-    if (HAS_SEQ) {
-#pragma unroll
-      for (int j = 0; j < H; ++j) {
-        const int nxt = __shfl_down_sync(kFull, sprev[j], 1);
-        srh[j] = lane == 31 ? srend[j] : nxt;
-      }
-      egated = !ids_uniform<H>(sprev, srh);
-    }
-    if (egated)
-      emit_dx_seq<T, W>(dprev, rh, sprev, srh, wp, tprev + 8 * lane, t1, dxa, a.dxs_c, va, vb);
-    else
-      emit_dx<T, W>(dprev, rh, wp, tprev + 8 * lane, t1, a, dxa, fa, va, vb);
   }
   // Warp sums of the dweight / dbias partials; lane 0 writes this item's slot.
 #pragma unroll
@@ -1388,16 +1346,39 @@ cudaError_t prepare(K kernel, size_t smem, std::atomic<uint64_t>& attr_done, std
 }
 
 // Items = (batch, group of 8 channels, segment); segments split long rows
-// when there are too few (batch, group) pairs to fill the GPU.
-void seq_schedule(const DeviceInfo& dev, int nb, i64 B, i64 D, i64 L, Plan* plan) {
+// when there are too few (batch, group) pairs to fill the GPU.  The launch
+// runs ceil(items / resident blocks) waves, each as long as a segment's
+// tiles plus a block's fixed start (barriers, weights, the halo and tail
+// loads, the pipeline fill: about kStartTiles tiles), so the segment count
+// minimises waves x (tiles per segment + kStartTiles).  One row of 256 tiles
+// over 512 pairs with 444 resident blocks: 2 segments run 2.3 waves (the
+// last a third full), 6 segments 6.9 waves.
+#ifndef CC1D_SEQ_START_TILES
+#define CC1D_SEQ_START_TILES 3
+#endif
+constexpr i64 kStartTiles = CC1D_SEQ_START_TILES;
+constexpr i64 kMaxSegs = 4096;  // bounds the host search
+
+// `step`: positions a tile advances (kTL, or kBwdStep for the overlapping
+// backward tiles); segments are whole numbers of steps.
+void seq_schedule(const DeviceInfo& dev, int nb, i64 B, i64 D, i64 L, i64 step, Plan* plan) {
   const i64 groups = ceil_div(D, (i64)kRows);
   const i64 pairs = B * groups;
-  const i64 target = 2 * (i64)dev.sms * nb;
-  i64 nseg = 1;
-  if (pairs < target) nseg = std::min<i64>(ceil_div(target, pairs), ceil_div(L, (i64)kTL));
-  if (nseg < 1) nseg = 1;
-  const i64 seg_len = ceil_div(ceil_div(L, nseg), (i64)kTL) * kTL;
-  nseg = ceil_div(L, seg_len);
+  const i64 resident = std::max<i64>(1, (i64)dev.sms * nb);
+  const i64 row_tiles = std::max<i64>(1, ceil_div(L, step));
+  i64 seg_tiles = row_tiles;
+  double best = -1.0;
+  for (i64 n = 1; n <= std::min(row_tiles, kMaxSegs); ++n) {
+    const i64 st = ceil_div(row_tiles, n);
+    const double cost = (double)ceil_div(pairs * ceil_div(row_tiles, st), resident) * (double)(st + kStartTiles);
+    if (best < 0.0 || cost < best) {
+      best = cost;
+      seg_tiles = st;
+    }
+    if (pairs * n >= 64 * resident) break;  // many waves already: splitting only adds starts
+  }
+  const i64 seg_len = seg_tiles * step;
+  const i64 nseg = ceil_div(L, seg_len);
   plan->layout = kSeq;
   plan->vec = true;
   plan->threads = kThreadsSeq;
@@ -1508,7 +1489,7 @@ struct SeqFwdOp {
     DeviceInfo dev;
     e = device_info(&dev);
     if (e != cudaSuccess) return e;
-    seq_schedule(dev, nb, a.B, a.D, a.L, plan);
+    seq_schedule(dev, nb, a.B, a.D, a.L, kTL, plan);
     plan->n_partials = 0;
     return cudaSuccess;
   }
@@ -1555,7 +1536,7 @@ struct SeqBwdOp {
     DeviceInfo dev;
     e = device_info(&dev);
     if (e != cudaSuccess) return e;
-    seq_schedule(dev, nb, a.B, a.D, a.L, plan);
+    seq_schedule(dev, nb, a.B, a.D, a.L, sh ? (i64)kTL : (i64)kBwdStep, plan);
     return cudaSuccess;
   }
 };

@@ -16,8 +16,9 @@
 //
 // The same semantics run in specialised kernels, chosen by the launcher
 // from the layout (every one issues all its loads before any store):
-//   update_vec_kernel      one token, linear, state_len W-1, packed or
-//                          channel-last pools: 4 channels per thread, vectors
+//   update_vec_kernel      one token: linear with state_len W-1 (packed or
+//                          channel-last pools) or circular channel-last
+//                          states; 4 channels per thread, vectors
 //   update_lin_kernel      linear, seqlen <= 8, state_len <= 16, any strides
 //   update_circ_row_kernel one token, circular, 16- or 32-byte state rows
 //   update_circ_kernel     one token, circular, any row size / strides
@@ -250,8 +251,14 @@ constexpr int kVecV = CC1D_VEC_V;
 // (only the state row waits for the pool index).
 // SCL: conv_state stored channel-last (unit channel stride): a thread's
 // state is W-1 runs of V channels, one per position, ss_l apart.
-template <typename T, int W, bool SCL>
+// CIRC (channel-last only): circular buffer of any state_len S >= W-1; the
+// window is the W-1 positions before cs = cache_seqlens[b] mod S and the new
+// token is written at cs (one run instead of W-1).  cs is loaded alongside
+// the pool index, so the state waits for one dependent round trip, as in the
+// linear pooled case.
+template <typename T, int W, bool SCL, bool CIRC = false>
 __global__ void __launch_bounds__(128, CC1D_VEC_MIN_BLOCKS) update_vec_kernel(const UpdateArgs a) {
+  static_assert(SCL || !CIRC, "circular mode is for channel-last states");
   griddep_wait();  // inputs and state may come from the previous kernel
   griddep_launch_dependents();
   constexpr int H = W - 1;
@@ -265,6 +272,7 @@ __global__ void __launch_bounds__(128, CC1D_VEC_MIN_BLOCKS) update_vec_kernel(co
   if (g >= groups) return;
   const i64 c0 = g * V;
   T* __restrict__ ob = static_cast<T*>(a.out) + b * a.os_b + c0;
+  const int cs_raw = CIRC ? a.cache_seqlens[b] : 0;  // in flight with the pool index
   i64 row = b;
   if (a.idx != nullptr) {
     const int r = a.idx[b];
@@ -304,15 +312,25 @@ __global__ void __launch_bounds__(128, CC1D_VEC_MIN_BLOCKS) update_vec_kernel(co
 #pragma unroll
     for (int e = 0; e < EW; ++e) wv[i + e] = pw.v[e];
   }
+  i64 cs = 0;  // circular write position
   if constexpr (SCL) {
+    i64 ui = 0;  // circular: position of window slot j
+    if constexpr (CIRC) {
+      cs = (i64)cs_raw % a.S;
+      if (cs < 0) cs += a.S;
+      ui = cs - H;
+      if (ui < 0) ui += a.S;
+    }
 #pragma unroll
     for (int j = 0; j < H; ++j) {
+      const T* sp = st + (CIRC ? ui : (i64)j) * a.ss_l;
 #pragma unroll
       for (int i = 0; i < V; i += EX) {
-        const Pack<T, EX> ps = ld_pack_rw<T, EX>(st + j * a.ss_l + i);
+        const Pack<T, EX> ps = ld_pack_rw<T, EX>(sp + i);
 #pragma unroll
         for (int e = 0; e < EX; ++e) sv[(i + e) * H + j] = ps.v[e];
       }
+      if constexpr (CIRC) ui = (ui + 1 == a.S) ? 0 : ui + 1;
     }
   } else {
 #pragma unroll
@@ -335,32 +353,42 @@ __global__ void __launch_bounds__(128, CC1D_VEC_MIN_BLOCKS) update_vec_kernel(co
   }
 #pragma unroll
   for (int i = 0; i < V; i += EX) st_pack<T, EX>(ob + i, po[i / EX]);
-  // New rows [old[1..H-1], x] for the V channels, packed back to vectors.
-  T nv[V * H];
+  if constexpr (CIRC) {
 #pragma unroll
-  for (int v = 0; v < V; ++v) {
+    for (int i = 0; i < V; i += EX) {
+      Pack<T, EX> pn;
 #pragma unroll
-    for (int j = 0; j < H - 1; ++j) nv[v * H + j] = sv[v * H + j + 1];
-    nv[v * H + H - 1] = xv[v];
-  }
-  if constexpr (SCL) {
-#pragma unroll
-    for (int j = 0; j < H; ++j) {
-#pragma unroll
-      for (int i = 0; i < V; i += EX) {
-        Pack<T, EX> pn;
-#pragma unroll
-        for (int e = 0; e < EX; ++e) pn.v[e] = nv[(i + e) * H + j];
-        st_pack<T, EX>(st + j * a.ss_l + i, pn);
-      }
+      for (int e = 0; e < EX; ++e) pn.v[e] = xv[i + e];
+      st_pack<T, EX>(st + cs * a.ss_l + i, pn);
     }
   } else {
+    // New rows [old[1..H-1], x] for the V channels, packed back to vectors.
+    T nv[V * H];
 #pragma unroll
-    for (int i = 0; i < V * H; i += ES) {
-      Pack<T, ES> pn;
+    for (int v = 0; v < V; ++v) {
 #pragma unroll
-      for (int e = 0; e < ES; ++e) pn.v[e] = nv[i + e];
-      st_pack<T, ES>(st + i, pn);
+      for (int j = 0; j < H - 1; ++j) nv[v * H + j] = sv[v * H + j + 1];
+      nv[v * H + H - 1] = xv[v];
+    }
+    if constexpr (SCL) {
+#pragma unroll
+      for (int j = 0; j < H; ++j) {
+#pragma unroll
+        for (int i = 0; i < V; i += EX) {
+          Pack<T, EX> pn;
+#pragma unroll
+          for (int e = 0; e < EX; ++e) pn.v[e] = nv[(i + e) * H + j];
+          st_pack<T, EX>(st + j * a.ss_l + i, pn);
+        }
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < V * H; i += ES) {
+        Pack<T, ES> pn;
+#pragma unroll
+        for (int e = 0; e < ES; ++e) pn.v[e] = nv[i + e];
+        st_pack<T, ES>(st + i, pn);
+      }
     }
   }
 }
@@ -628,26 +656,29 @@ bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) ==
 
 bool aligned_bytes(const void* p, i64 bytes) { return (reinterpret_cast<uintptr_t>(p) % (uintptr_t)bytes) == 0; }
 
-// Conditions of update_vec_kernel: one new token, linear mode with
-// state_len == W-1, (D, W) contiguous weights, unit channel stride for
-// x / out / bias, D a multiple of the channels per thread, and every run
-// aligned to the vector that moves it.  Returns 1 for packed state rows
-// (stride 1 over state_len, rows back to back), 2 for a channel-last state
-// (unit channel stride), 0 when the kernel does not apply.
+// Conditions of update_vec_kernel: one new token, (D, W) contiguous
+// weights, unit channel stride for x / out / bias, D a multiple of the
+// channels per thread, and every run aligned to the vector that moves it.
+// Returns 1 for linear mode with packed state rows (state_len == W-1, stride
+// 1 over state_len, rows back to back), 2 for linear mode with a channel-last
+// state (state_len == W-1, unit channel stride), 3 for circular mode with a
+// channel-last state (any state_len), 0 when the kernel does not apply
+// (circular packed rows go to update_circ_row_kernel).
 template <typename T, int W>
 int vec_path(const UpdateArgs& a) {
   constexpr int V = kVecV;
   constexpr i64 esz = (i64)sizeof(T);
   constexpr i64 EX = vec_elems<T, V>(), EW = vec_elems<T, V * W>(), ES = vec_elems<T, V * (W - 1)>();
-  const bool common = a.cache_seqlens == nullptr && a.L == 1 && a.D % V == 0 && a.S == W - 1 && a.ws_k == 1 &&
-                      a.ws_c == W && aligned_bytes(a.w, EW * esz) && a.xs_c == 1 && aligned_bytes(a.x, EX * esz) &&
-                      (a.B == 1 || a.xs_b % EX == 0) && a.os_c == 1 && aligned_bytes(a.out, EX * esz) &&
-                      (a.B == 1 || a.os_b % EX == 0) &&
+  const bool common = a.L == 1 && a.D % V == 0 && a.ws_k == 1 && a.ws_c == W && aligned_bytes(a.w, EW * esz) &&
+                      a.xs_c == 1 && aligned_bytes(a.x, EX * esz) && (a.B == 1 || a.xs_b % EX == 0) &&
+                      a.os_c == 1 && aligned_bytes(a.out, EX * esz) && (a.B == 1 || a.os_b % EX == 0) &&
                       (a.bias == nullptr || (a.bs == 1 && aligned_bytes(a.bias, EX * esz)));
   if (!common) return 0;
+  const bool chanlast = a.ss_c == 1 && aligned_bytes(a.state, EX * esz) && a.ss_l % EX == 0 && a.ss_b % EX == 0;
+  if (a.cache_seqlens != nullptr) return chanlast ? 3 : 0;
+  if (a.S != W - 1) return 0;
   if (a.ss_l == 1 && a.ss_c == a.S && aligned_bytes(a.state, ES * esz) && a.ss_b % ES == 0) return 1;
-  if (a.ss_c == 1 && aligned_bytes(a.state, EX * esz) && a.ss_l % EX == 0 && a.ss_b % EX == 0) return 2;
-  return 0;
+  return chanlast ? 2 : 0;
 }
 
 // Circular rows of 16 or 32 bytes, unit element stride, 16-byte aligned:
@@ -671,6 +702,7 @@ struct LaunchUpdate {
     const int vp = a.B <= 65535 ? vec_path<T, W>(a) : 0;
     if (vp != 0) {
       const dim3 grid((unsigned)ceil_div(a.D / kVecV, (i64)threads), (unsigned)a.B);
+      if (vp == 3) return launch_pdl(update_vec_kernel<T, W, true, true>, grid, dim3(threads), 0, stream, a);
       if (vp == 2) return launch_pdl(update_vec_kernel<T, W, true>, grid, dim3(threads), 0, stream, a);
       return launch_pdl(update_vec_kernel<T, W, false>, grid, dim3(threads), 0, stream, a);
     }

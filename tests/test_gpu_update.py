@@ -90,16 +90,20 @@ def test_decode_loop_matches_full_forward(dtype):
     assert torch.equal(full, dec)
 
 
+@pytest.mark.parametrize("chanlast", [False, True])  # conv_state (B, D, S) or stored (B, S, D)
 @pytest.mark.parametrize("row_bytes", [0, 16, 32])  # 0: state_len W-1; 16/32: whole-row kernel
 @pytest.mark.parametrize("dtype", ["fp32", "bf16"])
-def test_circular_decode_loop(dtype, row_bytes):
+def test_circular_decode_loop(dtype, row_bytes, chanlast):
     dt = DTYPES[dtype]
     B, D, L, W = 1, 8, 16, 4
     S = W - 1 if row_bytes == 0 else row_bytes // torch.tensor([], dtype=dt).element_size()
     x = torch.randn(B, D, L, dtype=dt, device=DEV)
     w = torch.randn(D, W, dtype=dt, device=DEV)
     full = causal_conv1d_fn(x, w, activation="silu")
-    state = torch.zeros(B, D, S, dtype=dt, device=DEV)
+    if chanlast:
+        state = torch.zeros(B, S, D, dtype=dt, device=DEV).transpose(1, 2)
+    else:
+        state = torch.zeros(B, D, S, dtype=dt, device=DEV)
     outs = []
     for t in range(L):
         cs = torch.tensor([t], dtype=torch.int32, device=DEV)
@@ -237,3 +241,37 @@ def test_linear_burst_and_state_layouts_vs_oracle(dtype, L, S, state_layout, poo
     assert_bitwise(st_g.cpu(), st_o, "conv_state")
     if idx is not None:
         assert torch.all(out[1] == 0)
+
+
+@pytest.mark.parametrize("pool", [False, True])
+@pytest.mark.parametrize("D", [1000, 1002])  # 1002: not a multiple of 4 channels -> generic circular kernel
+@pytest.mark.parametrize("dtype,W,S", [("bf16", 4, 3), ("bf16", 4, 8), ("bf16", 2, 1), ("fp16", 3, 13),
+                                       ("fp32", 4, 5), ("fp32", 2, 8)])
+def test_circular_chanlast_states_vs_oracle(dtype, W, S, D, pool):
+    """Circular decode with conv_state stored channel-last (strides (S*D, 1, D)
+    for each row; vLLM-style pools): the write head over its full range incl.
+    negative and wrapped values, any state_len >= W-1, pool rows addressed by
+    index with one padding entry.  Outputs within tolerance, state rows
+    bit-exact, padding and unused rows untouched."""
+    dt = DTYPES[dtype]
+    B = 7
+    rows = 2 * B if pool else B
+    x = seeded((B, D), dt, 31 + W)
+    w = seeded((D, W), dt, 32 + W, "uniform")
+    b = seeded((D,), dt, 33 + W, "uniform")
+    state = seeded((rows, D, S), dt, 34 + S)
+    cache = torch.tensor([0, 1, S - 1, S, 1023, -1, -S - 3], dtype=torch.int32)
+    idx = None
+    if pool:
+        idx = torch.randperm(rows, generator=torch.Generator().manual_seed(S))[:B].to(torch.int32)
+        idx[3] = -1
+    st_g = state.transpose(1, 2).contiguous().transpose(1, 2).to(DEV)
+    assert st_g.stride(1) == 1
+    out = causal_conv1d_update(x.to(DEV), st_g, w.to(DEV), b.to(DEV), activation="silu", cache_seqlens=cache.to(DEV),
+                               conv_state_indices=idx.to(DEV) if idx is not None else None)
+    st_o = state.clone()
+    o = oracle.update(x, st_o, w, b, silu=True, cache_seqlens=cache, conv_state_indices=idx)
+    assert_close(out.cpu(), o, dt, "out")
+    assert_bitwise(st_g.cpu(), st_o, "conv_state")
+    if idx is not None:
+        assert torch.all(out[3] == 0)
