@@ -197,8 +197,12 @@ cudaError_t plan_bwd_any(int dtype, int width, const BwdArgs& a, Plan* plan) {
                   : fam == 1 ? plan_bwd_tma(dtype, width, a, plan) : plan_bwd(dtype, width, a, plan);
 }
 
-size_t partial_bytes(const Plan& plan, int64_t dim, int width) {
-  return (size_t)plan.n_partials * (size_t)dim * (size_t)(width + 1) * sizeof(float);
+// Workspace of a backward plan: the dweight/dbias partials, then (256-byte
+// aligned) the plan's auxiliary bytes.
+size_t workspace_bytes(const Plan& plan, int64_t dim, int width) {
+  const size_t partials = (size_t)plan.n_partials * (size_t)dim * (size_t)(width + 1) * sizeof(float);
+  if (plan.aux_bytes == 0) return partials;
+  return (partials + 255) / 256 * 256 + (size_t)plan.aux_bytes;
 }
 
 }  // namespace
@@ -247,7 +251,7 @@ int cc1d_bwd_workspace_size(const cc1d_bwd_params* p, size_t* bytes) {
   std::memset(&plan, 0, sizeof(plan));
   cudaError_t e = plan_bwd_any(p->dtype, p->width, a, &plan);
   if (e != cudaSuccess) return cuda_fail(e, "cc1d_bwd plan");
-  *bytes = partial_bytes(plan, p->dim, p->width);
+  *bytes = workspace_bytes(plan, p->dim, p->width);
   return ok();
 }
 
@@ -278,7 +282,7 @@ int bwd_impl(const cc1d_bwd_params* p, const cc1d_peer_reduce* peer, void* strea
     const int fam = bwd_family(p->dtype, a);
     e = plan_bwd_any(p->dtype, p->width, a, &plan);
     if (e != cudaSuccess) return cuda_fail(e, "cc1d_bwd plan");
-    const size_t need = partial_bytes(plan, p->dim, p->width);
+    const size_t need = workspace_bytes(plan, p->dim, p->width);
     if (need > 0 && (p->workspace == nullptr || p->workspace_bytes < need))
       return fail(CC1D_ERR_WORKSPACE, "cc1d_bwd: workspace of %zu bytes needed, %zu given", need,
                   p->workspace == nullptr ? (size_t)0 : p->workspace_bytes);

@@ -29,6 +29,10 @@ struct Plan {
   i64 groups, splits, rows_per_split;
   // Backward: number of partial (dweight|dbias) sets per channel.
   i64 n_partials;
+  // Backward: bytes of workspace after the partials (256-byte aligned) for
+  // per-position data a kernel family derives from its inputs first (the
+  // seqlen kernels' sequence masks with seq_idx); 0 when none.
+  i64 aux_bytes;
 };
 
 struct FwdArgs {

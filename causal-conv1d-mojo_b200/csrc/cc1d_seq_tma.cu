@@ -58,7 +58,7 @@ namespace {
 #define CC1D_SEQ_BWD_MIN_BLOCKS 4  // widths <= 5: registers capped at 96, 4 blocks per SM (3 without: -16% at C5)
 #endif
 #ifndef CC1D_SEQ_BWD_IDS_MIN_BLOCKS
-#define CC1D_SEQ_BWD_IDS_MIN_BLOCKS 3  // with seq_idx (174 registers uncapped: 2 blocks per SM)
+#define CC1D_SEQ_BWD_IDS_MIN_BLOCKS 3  // with seq_idx (4 fits W <= 4 in 96 registers but measured 2% slower)
 #endif
 #ifndef CC1D_SEQ_FWD_SH_MIN_BLOCKS
 #define CC1D_SEQ_FWD_SH_MIN_BLOCKS 5  // shifted rows: <= 80 registers, 5 blocks per SM (the smem limit)
@@ -88,6 +88,54 @@ constexpr int seq_bwd_stages() {
 
 // Bytes of a stage's sequence-id tile (kTL int32 ids), present with seq_idx.
 constexpr unsigned kIdsBytes = kTL * sizeof(int);
+
+// Sequence masks (backward with seq_idx).  seq_mask_kernel runs first and
+// writes one uint16 per position q of each batch row: bit j (j < W-1) set
+// when position q-1-j exists and carries q's sequence id, bit 15 when q's id
+// is >= 0 (not padding).  A tap of the conv (or of its transpose) between
+// two positions counts exactly when the later position's mask has the bit of
+// their distance, so the backward reads one 16-byte mask vector per lane and
+// tile instead of ids and their halos, and a tile whose masks are all full
+// takes the ungated path.  Row pitch: L rounded up to 8 positions.
+constexpr unsigned kMaskBytes = kTL * sizeof(uint16_t);
+constexpr uint32_t kMaskValid = 0x8000u;
+template <int H>
+constexpr uint32_t mask_full() {
+  return ((1u << H) - 1u) | kMaskValid;
+}
+__host__ __device__ inline i64 mask_pitch(i64 L) { return (L + 7) / 8 * 8; }
+
+__global__ void __launch_bounds__(256) seq_mask_kernel(const int* __restrict__ seq, i64 ss_b, i64 ss_l, i64 B,
+                                                       i64 L, int H, uint16_t* __restrict__ mask) {
+  griddep_wait();  // seq_idx may come from the previous kernel; the mask buffer may still be read by it
+  griddep_launch_dependents();
+  const i64 Lp = mask_pitch(L);
+  const i64 q = (i64)blockIdx.x * blockDim.x + threadIdx.x;
+  if (q >= Lp) return;
+  for (i64 b = blockIdx.y; b < B; b += gridDim.y) {
+    uint32_t m = 0;
+    if (q < L) {
+      const int* sb = seq + b * ss_b;
+      const int id = sb[q * ss_l];
+      m = id >= 0 ? kMaskValid : 0u;
+      for (int j = 0; j < H; ++j) {
+        const i64 r = q - 1 - j;
+        if (r >= 0 && sb[r * ss_l] == id) m |= 1u << j;
+      }
+    }
+    mask[b * Lp + q] = (uint16_t)m;
+  }
+}
+
+// The 8 masks of a lane's positions as 4 words (position 2k in the low half
+// of word k), and the mask of position i (i < 8 compile-time).
+__device__ __forceinline__ void lds_masks(const unsigned char* tile, int lane, uint32_t (&m)[4]) {
+  const uint4 u = *reinterpret_cast<const uint4*>(tile + lane * 16);
+  m[0] = u.x; m[1] = u.y; m[2] = u.z; m[3] = u.w;
+}
+__device__ __forceinline__ uint32_t mask_at(const uint32_t (&m)[4], int i) {
+  return (m[i >> 1] >> (16 * (i & 1))) & 0xffffu;
+}
 
 // Shifted-row geometry (rows whose pitch is not a multiple of 16 bytes):
 // the tensor viewed as rows of `in` elements; a row tile is one box of
@@ -127,14 +175,13 @@ __device__ __forceinline__ void lds_ids(const unsigned char* ids, int lane, int 
 }
 
 // Halo ids of a lane (positions 8*lane-H .. 8*lane-1): from lane-1, or for
-// lane 0 from the previous tile (carry, updated to the last ids of lane
-// `last`, the last lane the next tile does not overlap).
+// lane 0 from the previous tile (carry, updated to this tile's last ids).
 template <int H>
-__device__ __forceinline__ void ids_halo(const int (&sid)[8], int (&carry)[H], int (&hs)[H], int lane, int last = 31) {
+__device__ __forceinline__ void ids_halo(const int (&sid)[8], int (&carry)[H], int (&hs)[H], int lane) {
 #pragma unroll
   for (int j = 0; j < H; ++j) {
     const int up = __shfl_up_sync(kFull, sid[8 - H + j], 1);
-    const int nc = __shfl_sync(kFull, sid[8 - H + j], last);
+    const int nc = __shfl_sync(kFull, sid[8 - H + j], 31);
     hs[j] = lane == 0 ? carry[j] : up;
     carry[j] = nc;
   }
@@ -411,21 +458,23 @@ __device__ __forceinline__ void emit_dx(const float2 (&d)[8], const float2 (&rh)
 }
 
 // emit_dx with seq_idx: dx at position q sums the taps of the outputs q+m
-// that carry q's sequence id (dpre is already 0 at padding).
+// that carry q's sequence id -- bit m-1 of the mask of q+m (dpre is already 0
+// at padding).  m: this lane's masks; rm: the masks of the next lane's first
+// positions (words 0 .. 3).
 template <typename T, int W>
-__device__ __forceinline__ void emit_dx_seq(const float2 (&d)[8], const float2 (&rh)[W - 1], const int (&sd)[8],
-                                            const int (&srh)[W - 1], const float2 (&wp)[W], i64 pos, bool store,
-                                            T* dxa, i64 dxs_c, bool va, bool vb) {
+__device__ __forceinline__ void emit_dx_mask(const float2 (&d)[8], const float2 (&rh)[W - 1], const uint32_t (&m)[4],
+                                             const uint32_t (&rm)[4], const float2 (&wp)[W], i64 pos, bool store,
+                                             T* dxa, i64 dxs_c, bool va, bool vb) {
   constexpr int H = W - 1;
   float ea[8], eb[8];
 #pragma unroll
   for (int i = 0; i < 8; ++i) {
     float2 acc = f2(0.f, 0.f);
 #pragma unroll
-    for (int m = 0; m <= H; ++m) {
-      const int q = i + m;
-      const int sq = q < 8 ? sd[q < 8 ? q : 0] : srh[q < 8 ? 0 : q - 8];
-      if (sq == sd[i]) acc = fma2(wp[H - m], q < 8 ? d[q < 8 ? q : 0] : rh[q < 8 ? 0 : q - 8], acc);
+    for (int k = 0; k <= H; ++k) {
+      const int q = i + k;
+      const uint32_t mq = q < 8 ? mask_at(m, q < 8 ? q : 0) : mask_at(rm, q < 8 ? 0 : q - 8);
+      if (k == 0 || ((mq >> (k - 1)) & 1u)) acc = fma2(wp[H - k], q < 8 ? d[q < 8 ? q : 0] : rh[q < 8 ? 0 : q - 8], acc);
     }
     ea[i] = acc.x;
     eb[i] = acc.y;
@@ -450,7 +499,7 @@ template <typename T, int W, bool HAS_SEQ, bool SILU>
 __global__ void __launch_bounds__(kThreadsSeq, W > 5 ? 1 : (HAS_SEQ ? CC1D_SEQ_BWD_IDS_MIN_BLOCKS : CC1D_SEQ_BWD_MIN_BLOCKS)) bwd_seq_tma_kernel(const __grid_constant__ SeqBwdParams p) {
   constexpr int H = W - 1;
   constexpr unsigned TB = seq_tile_bytes<T>();
-  constexpr unsigned SB = 2 * TB + (HAS_SEQ ? kIdsBytes : 0u);
+  constexpr unsigned SB = 2 * TB + (HAS_SEQ ? kMaskBytes : 0u);
   constexpr int NS = seq_bwd_stages<T>();
   extern __shared__ __align__(128) unsigned char smem[];
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + NS * SB);
@@ -510,13 +559,10 @@ __global__ void __launch_bounds__(kThreadsSeq, W > 5 ? 1 : (HAS_SEQ ? CC1D_SEQ_B
   const T* __restrict__ fa = a.dfin ? static_cast<const T*>(a.dfin) + b * a.fs_b + ra * a.fs_c : nullptr;
   T* __restrict__ dxa = static_cast<T*>(a.dx) + b * a.dxs_b + ra * a.dxs_c;
 
-  // Halo of lane 0 in the first tile: xc at t0-H .. t0-1 (and its ids).
+  // Halo of lane 0 in the first tile: xc at t0-H .. t0-1.
   float2 carry[H];
 #pragma unroll
   for (int j = 0; j < H; ++j) carry[j] = xc_pair(xr, a.xs_c, a.xs_l, ir, a.is_c, a.is_l, H, t0 - H + j, va, vb);
-  int scarry[H];
-#pragma unroll
-  for (int j = 0; j < H; ++j) scarry[j] = HAS_SEQ ? seq_at(a.seq + b * a.ss_b, a.ss_l, t0 - H + j, a.L) : 0;
 
   float2 dw[W];
 #pragma unroll
@@ -532,8 +578,8 @@ __global__ void __launch_bounds__(kThreadsSeq, W > 5 ? 1 : (HAS_SEQ ? CC1D_SEQ_B
     lds8<T>(smem + s * SB, 2 * warp + 1, lane, xb);
     lds8<T>(smem + s * SB + TB, 2 * warp, lane, ga);
     lds8<T>(smem + s * SB + TB, 2 * warp + 1, lane, gb);
-    int sid[8];
-    if (HAS_SEQ) lds_ids(smem + s * SB + 2 * TB, lane, sid);
+    uint32_t mk[4];
+    if (HAS_SEQ) lds_masks(smem + s * SB + 2 * TB, lane, mk);
     __syncwarp();
     if (lane == 0) mbar_arrive(&empty[s]);
     float2 xp[8], d[8];
@@ -548,11 +594,12 @@ __global__ void __launch_bounds__(kThreadsSeq, W > 5 ? 1 : (HAS_SEQ ? CC1D_SEQ_B
       h[j] = lane == 0 ? carry[j] : up;
       carry[j] = nc;
     }
-    int hs[H];
+    // Gated when any mask of the tile is not full.  A full tile also makes
+    // every dx tap of lanes 0..30 count (their right halos lie in the tile).
     bool gated = false;
     if (HAS_SEQ) {
-      ids_halo<H>(sid, scarry, hs, lane, 31 - 1);
-      gated = !ids_uniform<H>(sid, hs);
+      constexpr uint32_t kFull2 = mask_full<H>() * 0x10001u;
+      gated = !__all_sync(kFull, (mk[0] & mk[1] & mk[2] & mk[3]) == kFull2);
     }
     const i64 pos = t + 8 * lane;
     const bool own = lane < 31 && pos < t1;  // positions whose dx, dweight and dbias this tile produces
@@ -577,27 +624,28 @@ __global__ void __launch_bounds__(kThreadsSeq, W > 5 ? 1 : (HAS_SEQ ? CC1D_SEQ_B
         }
       }
     } else {
-      // Taps gated by sequence id; dpre is 0 at padding (id < 0).
+      // Tap kk of output i counts when mask bit H-1-kk of i is set (the
+      // position H-kk before it carries its id); dpre is 0 at padding.
 #pragma unroll
       for (int i = 0; i < 8; ++i) {
-        const int si = sid[i];
+        const uint32_t mi = mask_at(mk, i);
         float2 pre = bp;
 #pragma unroll
         for (int kk = 0; kk < W; ++kk) {
           const int q = i - H + kk;
-          const int sq = q >= 0 ? sid[q >= 0 ? q : 0] : hs[q >= 0 ? 0 : q + H];
-          if (sq == si) pre = fma2(wp[kk], q >= 0 ? xp[q >= 0 ? q : 0] : h[q >= 0 ? 0 : q + H], pre);
+          if (kk == H || ((mi >> (H - 1 - kk)) & 1u))
+            pre = fma2(wp[kk], q >= 0 ? xp[q >= 0 ? q : 0] : h[q >= 0 ? 0 : q + H], pre);
         }
         const float2 g = f2(ga[i], gb[i]);
         d[i] = SILU ? mul2(g, silu_grad2(pre)) : g;
-        if (si < 0) d[i] = f2(0.f, 0.f);
+        if (!(mi & kMaskValid)) d[i] = f2(0.f, 0.f);
         if (own) {
           db = add2(db, d[i]);
 #pragma unroll
           for (int kk = 0; kk < W; ++kk) {
             const int q = i - H + kk;
-            const int sq = q >= 0 ? sid[q >= 0 ? q : 0] : hs[q >= 0 ? 0 : q + H];
-            if (sq == si) dw[kk] = fma2(d[i], q >= 0 ? xp[q >= 0 ? q : 0] : h[q >= 0 ? 0 : q + H], dw[kk]);
+            if (kk == H || ((mi >> (H - 1 - kk)) & 1u))
+              dw[kk] = fma2(d[i], q >= 0 ? xp[q >= 0 ? q : 0] : h[q >= 0 ? 0 : q + H], dw[kk]);
           }
         }
       }
@@ -607,17 +655,14 @@ __global__ void __launch_bounds__(kThreadsSeq, W > 5 ? 1 : (HAS_SEQ ? CC1D_SEQ_B
     float2 rh[H];
 #pragma unroll
     for (int j = 0; j < H; ++j) rh[j] = shfl_down2(d[j], 1);
-    bool egated = false;
-    int srh[H];
-    if (HAS_SEQ) {
+    if (gated) {
+      uint32_t rm[4];
 #pragma unroll
-      for (int j = 0; j < H; ++j) srh[j] = __shfl_down_sync(kFull, sid[j], 1);
-      egated = !ids_uniform<H>(sid, srh);
-    }
-    if (egated)
-      emit_dx_seq<T, W>(d, rh, sid, srh, wp, pos, own, dxa, a.dxs_c, va, vb);
-    else
+      for (int w = 0; w < 4; ++w) rm[w] = 2 * w < H ? __shfl_down_sync(kFull, mk[w], 1) : 0u;
+      emit_dx_mask<T, W>(d, rh, mk, rm, wp, pos, own, dxa, a.dxs_c, va, vb);
+    } else {
       emit_dx<T, W>(d, rh, wp, pos, own, a, dxa, fa, va, vb);
+    }
     // dinitial_states: dpre of positions 0 .. H-1 live in lane 0 of tile 0.
     if (t == 0 && lane == 0 && a.dinit != nullptr) {
       T* di = static_cast<T*>(a.dinit) + b * a.dis_b + ra * a.dis_c;
@@ -1236,6 +1281,40 @@ bool make_ids_map(CUtensorMap* m, const int* base, i64 L, i64 B, i64 s_b) {
 
 // seq_idx that the id tiles can stream: unit position stride, 16-byte
 // aligned rows.
+// The sequence masks as (L, 1, B) uint16 with row pitch mask_pitch(L); box
+// (256, 1, 1), zero fill past L (a zero mask gates every tap).
+bool make_mask_map(CUtensorMap* m, const uint16_t* base, i64 L, i64 B) {
+  PFN_cuTensorMapEncodeTiled_v12000 enc = encode_fn();
+  if (enc == nullptr) return false;
+  const i64 pitch = mask_pitch(L) * (i64)sizeof(uint16_t);
+  cuuint64_t dims[3] = {(cuuint64_t)L, 1, (cuuint64_t)B};
+  cuuint64_t strides[2] = {(cuuint64_t)pitch, (cuuint64_t)pitch};
+  cuuint32_t box[3] = {(cuuint32_t)kTL, 1, 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  const CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_UINT16, 3, const_cast<uint16_t*>(base), dims, strides, box, estr,
+                         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    set_error_detail("cuTensorMapEncodeTiled returned %d for the sequence masks (L %lld, B %lld)", (int)r,
+                     (long long)L, (long long)B);
+  return r == CUDA_SUCCESS;
+}
+
+// Bytes of the sequence masks and their place in the workspace (after the
+// partials, 256-byte aligned; the plan's aux_bytes).
+i64 mask_bytes(i64 B, i64 L) { return B * mask_pitch(L) * (i64)sizeof(uint16_t); }
+uint16_t* mask_buffer(const BwdArgs& a, const Plan& plan, int W) {
+  const i64 partials = plan.n_partials * a.D * (i64)(W + 1) * (i64)sizeof(float);
+  return reinterpret_cast<uint16_t*>(reinterpret_cast<unsigned char*>(a.partials) + (partials + 255) / 256 * 256);
+}
+
+cudaError_t launch_seq_mask(const BwdArgs& a, int H, uint16_t* mask, cudaStream_t stream) {
+  const i64 blocks = ceil_div(mask_pitch(a.L), (i64)256);
+  if (blocks > 0x7fffffffLL) return cudaErrorInvalidConfiguration;
+  const dim3 grid((unsigned)blocks, (unsigned)std::min<i64>(a.B, 65535));
+  return launch_pdl(seq_mask_kernel, grid, dim3(256), 0, stream, a.seq, a.ss_b, a.ss_l, a.B, a.L, H, mask);
+}
+
 bool ids_ok(const int* seq, i64 s_l, i64 s_b, i64 B, i64 L) {
   return seq != nullptr && s_l == 1 && aligned_to(seq, 16) && (B == 1 || (s_b >= L && (s_b * 4) % 16 == 0)) &&
          (s_b * 4) < (1LL << 40);
@@ -1407,7 +1486,7 @@ cudaError_t seq_fwd_instance(SeqFwdParams* prm, const Plan* plan, cudaStream_t s
 
 template <typename T, int W, bool HAS_SEQ, bool SILU>
 cudaError_t seq_bwd_instance(SeqBwdParams* prm, const Plan* plan, cudaStream_t stream, int* nb_out) {
-  constexpr size_t smem = (size_t)seq_bwd_stages<T>() * (2 * seq_tile_bytes<T>() + (HAS_SEQ ? kIdsBytes : 0u)) +
+  constexpr size_t smem = (size_t)seq_bwd_stages<T>() * (2 * seq_tile_bytes<T>() + (HAS_SEQ ? kMaskBytes : 0u)) +
                           2 * seq_bwd_stages<T>() * sizeof(uint64_t);
   static std::atomic<uint64_t> attr{0};
   static std::atomic<int> occ{0};
@@ -1491,6 +1570,7 @@ struct SeqFwdOp {
     if (e != cudaSuccess) return e;
     seq_schedule(dev, nb, a.B, a.D, a.L, kTL, plan);
     plan->n_partials = 0;
+    plan->aux_bytes = 0;
     return cudaSuccess;
   }
 };
@@ -1518,7 +1598,13 @@ struct SeqBwdOp {
                          : (make_seq_map<T>(&storage.map_x, a.x, a.L, a.D, a.B, a.xs_c, a.xs_b) &&
                             make_seq_map<T>(&storage.map_g, a.dout, a.L, a.D, a.B, a.gs_c, a.gs_b));
       if (!ok) return cudaErrorInvalidValue;
-      if (a.seq != nullptr && !make_ids_map(&storage.map_s, a.seq, a.L, a.B, a.ss_b)) return cudaErrorInvalidValue;
+      if (a.seq != nullptr) {
+        // The backward reads sequence masks, written just before it.
+        uint16_t* mask = mask_buffer(a, *plan, W);
+        if (!make_mask_map(&storage.map_s, mask, a.L, a.B)) return cudaErrorInvalidValue;
+        const cudaError_t em = launch_seq_mask(a, W - 1, mask, stream);
+        if (em != cudaSuccess) return em;
+      }
       prm = &storage;
     }
     int nb = 1;
@@ -1537,6 +1623,7 @@ struct SeqBwdOp {
     e = device_info(&dev);
     if (e != cudaSuccess) return e;
     seq_schedule(dev, nb, a.B, a.D, a.L, sh ? (i64)kTL : (i64)kBwdStep, plan);
+    plan->aux_bytes = (!sh && a.seq != nullptr) ? mask_bytes(a.B, a.L) : 0;
     return cudaSuccess;
   }
 };
