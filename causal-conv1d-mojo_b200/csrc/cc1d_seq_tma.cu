@@ -64,7 +64,7 @@ namespace {
 #define CC1D_SEQ_FWD_SH_MIN_BLOCKS 5  // shifted rows: <= 80 registers, 5 blocks per SM (the smem limit)
 #endif
 #ifndef CC1D_SEQ_BWD_SH_MIN_BLOCKS
-#define CC1D_SEQ_BWD_SH_MIN_BLOCKS 3  // shifted rows (4 spills ~200 bytes at W = 4)
+#define CC1D_SEQ_BWD_SH_MIN_BLOCKS 4  // shifted rows (overlapping tiles: 8 bytes of spills at W = 4)
 #endif
 
 constexpr int kSW = CC1D_SEQ_WARPS;  // consumer warps
@@ -145,8 +145,9 @@ struct ShiftGeom {
   int in_log2;
   int rows;      // kTL / in + 1
   unsigned tx;   // bytes one tensor's tile delivers (kRows boxes)
-  // Tiles of a segment: seg_len / kTL, and for a row's last segment enough
-  // to reach L from its start - (E - 1).  Counted on the host.
+  // Tiles of a segment: seg_len / step (step = the positions a tile
+  // advances: kTL forward, kBwdStep backward), and for a row's last segment
+  // enough to reach L from its start - (E - 1).  Counted on the host.
   int tiles_full, tiles_last;
 };
 
@@ -992,6 +993,11 @@ __device__ __forceinline__ void emit_dx_shift(const float2 (&d)[8], const float2
   if (vb) stg8_rowpos<T>(dxa + a.xs_c, qb, L, eb);
 }
 
+// Like bwd_seq_tma_kernel, the tiles overlap by one lane (they advance
+// kBwdStep = 248 positions): lanes 0..30 own their positions, lane 31
+// recomputes the dpre lane 30's dx needs, and each tile's dx is emitted in
+// the tile.  A tile's first element then sits at a different offset of its
+// box from tile to tile (248 is not a multiple of the view row).
 template <typename T, int W, bool SILU>
 __global__ void __launch_bounds__(kThreadsSeq, W > 5 ? 1 : CC1D_SEQ_BWD_SH_MIN_BLOCKS) bwd_shift_tma_kernel(const __grid_constant__ SeqBwdParams p) {
   constexpr int H = W - 1;
@@ -1037,7 +1043,7 @@ __global__ void __launch_bounds__(kThreadsSeq, W > 5 ? 1 : CC1D_SEQ_BWD_SH_MIN_B
         const unsigned s = k % NS, use = k / NS;
         if (use > 0 && !mbar_wait(&empty[s], (use - 1) & 1)) break;  // consumers stopped
         mbar_arrive_expect_tx(&full[s], 2 * p.sg.tx);
-        const int t = t0 + k * kTL;
+        const int t = t0 + k * kBwdStep;
         shift_load_rows(smem + s * SB, RB, &p.map_x, &full[s], rbase, a.xs_c, t, E, p.sg.in_log2);
         shift_load_rows(smem + s * SB + TB, RB, &p.map_g, &full[s], rbase, a.xs_c, t, E, p.sg.in_log2);
       }
@@ -1057,8 +1063,10 @@ __global__ void __launch_bounds__(kThreadsSeq, W > 5 ? 1 : CC1D_SEQ_BWD_SH_MIN_B
   const float2 bp = f2((bias && va) ? Cvt<T>::f(bias[ra * a.bs]) : 0.f, (bias && vb) ? Cvt<T>::f(bias[(ra + 1) * a.bs]) : 0.f);
   const i64 Ra = b * a.xs_b + ra * a.xs_c, Rb = Ra + a.xs_c;
   const int off_a = (int)(Ra & (E - 1)), off_b = (int)(Rb & (E - 1));
-  const unsigned o2a = (unsigned)((Ra & (p.sg.in - 1)) - off_a) * sizeof(T);
-  const unsigned o2b = (unsigned)((Rb & (p.sg.in - 1)) - off_b) * sizeof(T);
+  // Low bits of each row's aligned start: with the tile's start they give the
+  // tile's first element within its box.
+  const unsigned ba = (unsigned)(Ra - off_a), bb = (unsigned)(Rb - off_b);
+  const unsigned inm = (unsigned)p.sg.in - 1u;
   const T* __restrict__ xr = static_cast<const T*>(a.x) + Ra;
   const T* __restrict__ gr = static_cast<const T*>(a.dout) + Ra;
   const T* __restrict__ ir = a.init ? static_cast<const T*>(a.init) + b * a.is_b + ra * a.is_c : nullptr;
@@ -1096,14 +1104,14 @@ __global__ void __launch_bounds__(kThreadsSeq, W > 5 ? 1 : CC1D_SEQ_BWD_SH_MIN_B
 #pragma unroll
   for (int k = 0; k < W; ++k) dw[k] = f2(0.f, 0.f);
   float2 db = f2(0.f, 0.f);
-  float2 dprev[8];
-  int qpa = 0, qpb = 0;  // row positions of dprev's element 0
+  const bool owner = lane < 31;
 
   for (int k = 0; k < ntiles; ++k) {
     const unsigned s = k % NS, use = k / NS;
     if (!mbar_wait(&full[s], use & 1)) return;
-    unsigned char* rowa = smem + s * SB + (2 * warp) * RB + o2a;
-    unsigned char* rowb = smem + s * SB + (2 * warp + 1) * RB + o2b;
+    const unsigned t = (unsigned)(t0 + k * kBwdStep);
+    unsigned char* rowa = smem + s * SB + (2 * warp) * RB + ((ba + t) & inm) * sizeof(T);
+    unsigned char* rowb = smem + s * SB + (2 * warp + 1) * RB + ((bb + t) & inm) * sizeof(T);
     if (t0 == 0 && k == 0) {
       if (lane == 0) {
         if (va) fix_row_head<T>(rowa, off_a, ir, a.is_l, H);
@@ -1119,7 +1127,7 @@ __global__ void __launch_bounds__(kThreadsSeq, W > 5 ? 1 : CC1D_SEQ_BWD_SH_MIN_B
     lds8_row<T>(rowb + TB, lane, gb);
     __syncwarp();
     if (lane == 0) mbar_arrive(&empty[s]);
-    const int qa = qa0 + k * kTL, qb = qb0 + k * kTL;
+    const int qa = qa0 + k * kBwdStep, qb = qb0 + k * kBwdStep;
     float2 xp[8], d[8];
 #pragma unroll
     for (int i = 0; i < 8; ++i) xp[i] = f2(xa[i], xb[i]);
@@ -1127,7 +1135,7 @@ __global__ void __launch_bounds__(kThreadsSeq, W > 5 ? 1 : CC1D_SEQ_BWD_SH_MIN_B
 #pragma unroll
     for (int j = 0; j < H; ++j) {
       const float2 up = shfl_up2(xp[8 - H + j], 1);
-      const float2 nc = shfl2(xp[8 - H + j], 31);
+      const float2 nc = shfl2(xp[8 - H + j], 31 - 1);
       h[j] = lane == 0 ? carry[j] : up;
       carry[j] = nc;
     }
@@ -1147,40 +1155,20 @@ __global__ void __launch_bounds__(kThreadsSeq, W > 5 ? 1 : CC1D_SEQ_BWD_SH_MIN_B
         if (qa + i < 0 || qa + i >= L) d[i].x = 0.f;
         if (qb + i < 0 || qb + i >= L) d[i].y = 0.f;
       }
-      db = add2(db, d[i]);
+      if (owner) {
+        db = add2(db, d[i]);
 #pragma unroll
-      for (int kk = 0; kk < W; ++kk) {
-        const int q = i - H + kk;
-        dw[kk] = fma2(d[i], q >= 0 ? xp[q >= 0 ? q : 0] : h[q >= 0 ? 0 : q + H], dw[kk]);
+        for (int kk = 0; kk < W; ++kk) {
+          const int q = i - H + kk;
+          dw[kk] = fma2(d[i], q >= 0 ? xp[q >= 0 ? q : 0] : h[q >= 0 ? 0 : q + H], dw[kk]);
+        }
       }
     }
-    // dx of the previous tile: lane 31 now has its right halo.
-    if (k > 0) {
-      float2 rh[H];
-#pragma unroll
-      for (int j = 0; j < H; ++j) {
-        const float2 nxt = shfl_down2(dprev[j], 1);
-        const float2 first = shfl2(d[j], 0);
-        rh[j] = lane == 31 ? first : nxt;
-      }
-      emit_dx_shift<T, W>(dprev, rh, wp, qpa, qpb, L, a, dxa, fa, va, vb);
-    }
-#pragma unroll
-    for (int i = 0; i < 8; ++i) dprev[i] = d[i];
-    qpa = qa;
-    qpb = qb;
-  }
-  if (ntiles > 0) {
-    // dpre just past each row's segment (0 past the row), for lane 31's last dx.
-    const int ea = last_seg ? L : t0 + seg_len - off_a, eb = last_seg ? L : t0 + seg_len - off_b;
+    // dx of this tile: the right halo of lane l is lane l + 1's first dpre.
     float2 rh[H];
 #pragma unroll
-    for (int j = 0; j < H; ++j) {
-      const float2 nxt = shfl_down2(dprev[j], 1);
-      const float2 e = dpre_rows<T, W, SILU>(xr, gr, ir, a, wp, bp, ea + j, eb + j, va, vb);
-      rh[j] = lane == 31 ? e : nxt;
-    }
-    emit_dx_shift<T, W>(dprev, rh, wp, qpa, qpb, L, a, dxa, fa, va, vb);
+    for (int j = 0; j < H; ++j) rh[j] = shfl_down2(d[j], 1);
+    emit_dx_shift<T, W>(d, rh, wp, qa, qb, L, a, dxa, fa, va && owner, vb && owner);
   }
   // Warp sums of the dweight / dbias partials; lane 0 writes this item's slot.
 #pragma unroll
@@ -1332,10 +1320,10 @@ i64 sh_extent(i64 B, i64 D, i64 L, i64 s_c, i64 s_b) { return (B - 1) * s_b + (D
 // elements, 16 .. kShMaxRowBytes bytes, that divides the extent (sh_ok
 // guarantees 16 bytes does); and the tile counts of the segments.
 template <typename T>
-ShiftGeom sh_geom(i64 extent, i64 L, i64 nseg, i64 seg_len) {
+ShiftGeom sh_geom(i64 extent, i64 L, i64 nseg, i64 seg_len, i64 step) {
   ShiftGeom g;
-  g.tiles_full = (int)(seg_len / kTL);
-  g.tiles_last = (int)ceil_div(L - (nseg - 1) * seg_len + unit_elems<T>() - 1, (i64)kTL);
+  g.tiles_full = (int)(seg_len / step);
+  g.tiles_last = (int)ceil_div(L - (nseg - 1) * seg_len + unit_elems<T>() - 1, step);
   int in = kShMaxRowBytes / (int)sizeof(T);
   while (in > unit_elems<T>() && extent % in != 0) in >>= 1;
   g.in = in;
@@ -1546,7 +1534,7 @@ struct SeqFwdOp {
       storage.a.seg_len = plan->seg_len;
       storage.groups = plan->groups;
       const i64 ext = sh_extent(a.B, a.D, a.L, a.xs_c, a.xs_b);
-      storage.sg = sh_geom<T>(ext, a.L, plan->nseg, plan->seg_len);
+      storage.sg = sh_geom<T>(ext, a.L, plan->nseg, plan->seg_len, kTL);
       const bool ok = sh ? make_sh_map<T>(&storage.map_x, a.x, ext, storage.sg)
                          : make_seq_map<T>(&storage.map_x, a.x, a.L, a.D, a.B, a.xs_c, a.xs_b);
       if (!ok) return cudaErrorInvalidValue;
@@ -1592,7 +1580,7 @@ struct SeqBwdOp {
       storage.a.seg_len = plan->seg_len;
       storage.groups = plan->groups;
       const i64 ext = sh_extent(a.B, a.D, a.L, a.xs_c, a.xs_b);
-      storage.sg = sh_geom<T>(ext, a.L, plan->nseg, plan->seg_len);
+      storage.sg = sh_geom<T>(ext, a.L, plan->nseg, plan->seg_len, kBwdStep);
       const bool ok = sh ? (make_sh_map<T>(&storage.map_x, a.x, ext, storage.sg) &&
                             make_sh_map<T>(&storage.map_g, a.dout, ext, storage.sg))
                          : (make_seq_map<T>(&storage.map_x, a.x, a.L, a.D, a.B, a.xs_c, a.xs_b) &&
@@ -1622,7 +1610,7 @@ struct SeqBwdOp {
     DeviceInfo dev;
     e = device_info(&dev);
     if (e != cudaSuccess) return e;
-    seq_schedule(dev, nb, a.B, a.D, a.L, sh ? (i64)kTL : (i64)kBwdStep, plan);
+    seq_schedule(dev, nb, a.B, a.D, a.L, kBwdStep, plan);
     plan->aux_bytes = (!sh && a.seq != nullptr) ? mask_bytes(a.B, a.L) : 0;
     return cudaSuccess;
   }
