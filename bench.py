@@ -650,6 +650,55 @@ def decode_sweep(w, b, rn, peak):
     return out
 
 
+def time_decode_sharded(world, rank, peak):
+    """Decode rows of the multi-GPU table: causal_conv1d_update batch-sharded,
+    no collective (pool slots stay on their GPU).  Every rank serves its own
+    C3a batch (256 requests on a pool of 512 slots, indexed) and C3b batch
+    (256 circular states of 8), weak scaling; each op is a CUDA graph of 8
+    launches over rotating buffer sets (> L2), and the time is the max over
+    ranks."""
+    from causal_conv1d_b200 import _ops
+
+    g = torch.Generator(device="cuda").manual_seed(100 + rank)
+    Bu, Du, sets = 256, D, 8
+
+    def rn(*s):
+        return torch.randn(*s, generator=g, device="cuda", dtype=torch.float32).to(DT)
+
+    w = (torch.rand(Du, W, generator=g, device="cuda") - 0.5).to(DT)
+    bias = (torch.rand(Du, generator=g, device="cuda") - 0.5).to(DT)
+    xs = [rn(Bu, Du, 1) for _ in range(sets)]
+    outs = [torch.empty_like(xs[0]) for _ in range(sets)]
+    pools = [rn(2 * Bu, Du, W - 1) for _ in range(sets)]
+    idx = [torch.randperm(2 * Bu, device="cuda", generator=g)[:Bu].to(torch.int32) for _ in range(sets)]
+    states = [rn(Bu, Du, 8) for _ in range(sets)]
+    cache = [torch.randint(0, 1024, (Bu,), device="cuda", dtype=torch.int32, generator=g) for _ in range(sets)]
+    ops = {
+        "c3a_indexed": (lambda i: _ops.update(xs[i], pools[i], w, bias, None, idx[i], outs[i], True),
+                        Bu * Du * (2 + 2 + 6 + 6) + Du * (W + 1) * 2 + Bu * 4),
+        "c3b_circular": (lambda i: _ops.update(xs[i], states[i], w, bias, cache[i], None, outs[i], True),
+                         Bu * Du * (2 + 2 + 6 + 2) + Du * (W + 1) * 2 + Bu * 4),
+    }
+    res = {"workload": f"causal_conv1d_update batch-sharded: each GPU its own ({Bu}, {Du}) bf16 decode batch "
+                       f"(weak scaling, no collective)", "n_gpus": world}
+    for name, (fn, nbytes) in ops.items():
+        for i in range(sets):
+            fn(i)
+        torch.cuda.synchronize()
+        gr = graph_of(fn, sets)
+        graph_ms(gr, 20, sets)  # warm-up replays
+        ms = graph_ms(gr, 100, sets)  # no cross-rank dependency: each GPU timed on its own
+        per = [v[0] for v in gather_floats([ms], world)]
+        t = max(per)
+        res[name] = {"ms_per_launch_max_over_ranks": t, "per_rank_ms": per,
+                     "tokens_per_s": world * Bu / (t / 1e3), "frac_per_gpu": nbytes / t / 1e6 / peak,
+                     "algorithmic_bytes_per_gpu": nbytes}
+        del gr
+    del xs, outs, pools, idx, states, cache
+    torch.cuda.empty_cache()
+    return res
+
+
 def peak_tflops():
     p = REPO / "MEASURED_PEAKS.json"
     if p.is_file():
@@ -1057,6 +1106,7 @@ def main():
     ap.add_argument("--skip-e2e", action="store_true")
     ap.add_argument("--skip-cpu", action="store_true")
     ap.add_argument("--skip-c5", action="store_true", help="skip the C5 sweep (BASELINE configs[4])")
+    ap.add_argument("--skip-decode", action="store_true", help="skip the batch-sharded decode rows")
     ap.add_argument("--only", default=None,
                     help="launch one op alone (fwd_c2, bwd_c2, update_c3a, update_c3b, update_burst4, "
                          "update_c3a_chanlast, update_c3b_chanlast, fwd_c4, bwd_c4, fwd_c5, bwd_c5) --reps times, for profilers; "
@@ -1085,6 +1135,7 @@ def main():
     r = time_c2(args, world, rank, reducer)
     e2e = None if args.skip_e2e else time_e2e(args, world, rank, reducer)
     c5 = None if args.skip_c5 else time_c5_sweep(world, rank, local, peak)
+    decode = None if args.skip_decode else time_decode_sharded(world, rank, peak)
     kernels = None
     if rank == 0 and not args.skip_kernels:
         kernels = time_kernels(peak)
@@ -1145,6 +1196,8 @@ def main():
             line["per_rank"] = r["per_rank"]
         if c5 is not None:
             line["c5_sweep"] = c5
+        if decode is not None:
+            line["decode_sharded"] = decode
         if e2e is not None:
             line["e2e"] = e2e
         if cpu is not None:

@@ -86,7 +86,9 @@ CC1D_API int cc1d_fwd(const cc1d_fwd_params* params, void* stream);
  *
  * dweight/dbias: the kernel writes per-block partial sums into `workspace`
  * (size from cc1d_bwd_workspace_size) and a second kernel reduces them in a
- * fixed order -- results are bitwise reproducible run to run.  The reduced
+ * fixed order -- results are bitwise reproducible run to run.  With seq_idx
+ * on seqlen-contiguous data the workspace also holds per-position sequence
+ * masks that a first kernel derives from seq_idx.  The reduced
  * fp32 sums are OVERWRITTEN (not accumulated) into `dwdb_acc`, a contiguous
  * fp32 buffer of dim*(W+1) floats laid out as [dweight (dim, W) | dbias (dim)]
  * so that one all-reduce covers both when the batch is sharded across GPUs.

@@ -253,6 +253,34 @@ def test_seq_idx_long_runs_vs_oracle(dtype, W, layout):
     _compare_oracle(x, w, b, seq, None, dout, None, True, False, layout)
 
 
+@pytest.mark.parametrize("layout", ["contig", "chanlast"])
+@pytest.mark.parametrize("W", [3, 4])
+@pytest.mark.parametrize("dtype", ["fp32", "bf16"])
+def test_seq_idx_reused_ids_and_step_edges_vs_oracle(dtype, W, layout):
+    """seq_idx whose boundaries sit on and next to the contiguous backward's
+    248-position tile steps, an id that comes back after a one- or
+    two-position run of another id (taps compare ids, so a tap may reach
+    across the short run), padding between runs of one id, and a row
+    (second batch row) that is one sequence throughout."""
+    dt = DTYPES[dtype]
+    B, D, L = 2, 40, 2976  # 12 steps of 248
+    seed = 57 + W
+    x = seeded((B, D, L), dt, seed)
+    w = seeded((D, W), dt, seed + 1, "uniform")
+    b = seeded((D,), dt, seed + 2, "uniform")
+    dout = seeded((B, D, L), dt, seed + 4)
+    runs = [(248, 0), (1, 1), (247, 0), (248, 2), (2, 3), (250, 2), (1, -1), (495, 4), (3, -1), (248, 4), (1, 5),
+            (1, 4), (1, 5), (1230, 6)]
+    seq = torch.empty(B, L, dtype=torch.int32)
+    t = 0
+    for n, v in runs:
+        seq[0, t:t + n] = v
+        t += n
+    assert t == L
+    seq[1] = 7
+    _compare_oracle(x, w, b, seq, None, dout, None, True, False, layout)
+
+
 @pytest.mark.parametrize("W", [5, 6, 7, 8, 9])
 @pytest.mark.parametrize("layout", ["contig", "chanlast"])
 def test_wide_widths_vs_oracle(W, layout):
