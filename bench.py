@@ -239,8 +239,18 @@ def graph_ms(g, reps, per_graph):
     return a.elapsed_time(c) / (reps * per_graph)
 
 
-def time_c2(args, world, rank, reducer):
-    from causal_conv1d_b200 import _ops
+def time_c2(args, world, rank, reducer, split=None):
+    """The headline step: C2 forward + backward.  With N GPUs each rank's
+    backward sums dweight/dbias over the ranks through NVLink peer memory.
+    The K timed steps run twice at N > 1: with the fused exchange
+    (`reducer`: the reduction kernel pushes, waits for the peers and writes
+    the sums) and with the split exchange (`split`: the backward pushes, and
+    the wait plus the output writes run after the next step's forward, when
+    the peers' sums have had the whole forward to arrive -- the pattern of a
+    training loop that reads the gradients only at the optimizer step; every
+    step still does one PUSH and one FINISH).  Each is timed as max over
+    ranks; the faster is the job's step and both are reported."""
+    from causal_conv1d_b200 import _lib, _ops
 
     x, w, b, init, dout = make_c2(1234 + rank, "cuda")
     out = torch.empty_like(x)
@@ -267,20 +277,17 @@ def time_c2(args, world, rank, reducer):
         fwd()
         bwd()
 
-    with Clocks(torch.cuda.current_device()) as clk:
-        # The sampler starts before the warm-up so that it is already
-        # reporting when the timed steps run.
+    def timed(step_fn):
+        """Warm-up, then EXACTLY K steps replayed from a CUDA graph (captured
+        once, as a serving / training loop would), between a device-side
+        rendezvous and a synchronize; this rank's milliseconds."""
         for _ in range(args.warmup):
-            step()
+            step_fn()
         torch.cuda.synchronize()
-        # The timed step is replayed from a CUDA graph (captured once), as a
-        # serving / training loop would; every replay launches the same
-        # kernels on the same buffers.
-        g_step = graph_of(step)
+        g_step = graph_of(step_fn)
         for _ in range(args.warmup):
             g_step.replay()
         barrier_sync(world)
-        clk.mark()
         device_rendezvous(world)
         start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         start.record()
@@ -288,9 +295,44 @@ def time_c2(args, world, rank, reducer):
             g_step.replay()
         stop.record()
         torch.cuda.synchronize()
-        clk.unmark()
         barrier_sync(world)
-    total_ms = start.elapsed_time(stop)
+        del g_step
+        return start.elapsed_time(stop)
+
+    exchange = {}
+    with Clocks(torch.cuda.current_device()) as clk:
+        # The sampler starts before the warm-up so that it is already
+        # reporting when the timed steps run.
+        clk.mark()
+        total_ms = timed(step)
+        if split is not None:
+            # The same K steps with the split exchange; the faster of the two
+            # (max over ranks each) is the job's step.
+            def push():
+                _ops.bwd_peer(x, w, b, dout, init, None, dx, dwdb, dinit, dw, db, True,
+                              *split.args(_lib.PEER_PUSH))
+
+            def finish():
+                _ops.bwd_peer(x, w, b, dout, init, None, dx, dwdb, dinit, dw, db, True,
+                              *split.args(_lib.PEER_FINISH))
+
+            def split_step(_=0):
+                fwd()
+                finish()  # the previous step's exchange (FINISH before the next PUSH)
+                push()
+
+            fwd()
+            push()  # the first step has no previous exchange to finish
+            split_ms = timed(split_step)
+            finish()  # the last step's exchange
+            torch.cuda.synchronize()
+            split.check()
+            fused_max, split_max = max_over_ranks(total_ms, world), max_over_ranks(split_ms, world)
+            exchange = {"fused_ms_per_step": fused_max / K, "split_ms_per_step": split_max / K,
+                        "used": "split" if split_max < fused_max else "fused"}
+            if split_max < fused_max:
+                total_ms = split_ms
+        clk.unmark()
     # Per-op kernel times: graphs of the op alone, replayed back to back.
     reps = max(20, min(200, K // 10))
     g_fwd, g_bwd = graph_of(fwd, 10), graph_of(bwd, 10)
@@ -300,7 +342,7 @@ def time_c2(args, world, rank, reducer):
     barrier_sync(world)
     device_rendezvous(world)
     bwd_ms = graph_ms(g_bwd, reps, 10)
-    del g_step, g_fwd, g_bwd
+    del g_fwd, g_bwd
     barrier_sync(world)
     extra = {}
     if world > 1:
@@ -319,16 +361,29 @@ def time_c2(args, world, rank, reducer):
             _ops.bwd(x, w, b, dout, None, init, None, l_dx, l_dwdb, l_dinit, l_dw, l_db, True)
 
         local_ms = graph_ms(graph_of(local_step, 10), reps, 10)
-        per_rank = gather_floats([total_ms / K, bwd_ms, local_ms], world)
+
+        def fused_step(_=0):
+            fwd()
+            bwd()
+
+        barrier_sync(world)
+        device_rendezvous(world)
+        fused_ms = graph_ms(graph_of(fused_step, 10), reps, 10)
+        per_rank = gather_floats([total_ms / K, bwd_ms, local_ms, fused_ms], world)
         extra["per_rank"] = {
             "step_ms": [r[0] for r in per_rank],
             "bwd_with_exchange_ms": [r[1] for r in per_rank],
             "step_local_reduction_ms": [r[2] for r in per_rank],
-            "note": "step_local_reduction_ms: the same fwd+bwd with the dweight/dbias reduction kept on the "
+            "step_fused_exchange_ms": [r[3] for r in per_rank],
+            "note": "step_ms: the timed step (the faster exchange, see `exchange`); bwd_with_exchange_ms: the backward alone with the fused exchange; "
+                    "step_fused_exchange_ms: fwd+bwd with the fused exchange (waiting inside the reduction "
+                    "kernel); step_local_reduction_ms: the same fwd+bwd with the dweight/dbias reduction kept on the "
                     "rank (no exchange); its max over ranks bounds a synchronous step from below",
         }
     extra["parity_c2"] = c2_parity(x, w, b, init, dout, out, fs, dx, dinit, dw, db) if rank == 0 else None
     total_ms = max_over_ranks(total_ms, world)
+    if exchange:
+        extra["exchange"] = exchange
     return dict(ms_per_step=total_ms / K, fwd_ms=fwd_ms, bwd_ms=bwd_ms, clocks=clk.summary(), **extra)
 
 
@@ -1127,12 +1182,13 @@ def main():
     peak, peak_kind = peaks()
     fwd_bytes, bwd_bytes = c2_bytes()
 
-    reducer = None
+    reducer = split_reducer = None
     if world > 1:
         from causal_conv1d_b200.parallel import PeerReducer
 
         reducer = PeerReducer(D, W, torch.device("cuda", local))
-    r = time_c2(args, world, rank, reducer)
+        split_reducer = PeerReducer(D, W, torch.device("cuda", local))
+    r = time_c2(args, world, rank, reducer, split_reducer)
     e2e = None if args.skip_e2e else time_e2e(args, world, rank, reducer)
     c5 = None if args.skip_c5 else time_c5_sweep(world, rank, local, peak)
     decode = None if args.skip_decode else time_decode_sharded(world, rank, peak)
@@ -1187,13 +1243,15 @@ def main():
                 "algorithmic_bytes_per_launch": bwd_bytes,
             },
             "kernels": ktab,
-            "gpu_launches": 3 * args.steps,
+            "gpu_launches": (4 if r.get("exchange", {}).get("used") == "split" else 3) * args.steps,
             "clocks": r["clocks"],
             "parity": {k: v for k, v in (("peer_reduction", r.get("parity")), ("c2_step", r.get("parity_c2")))
                        if v is not None},
         }
         if "per_rank" in r:
             line["per_rank"] = r["per_rank"]
+        if "exchange" in r:
+            line["exchange"] = r["exchange"]
         if c5 is not None:
             line["c5_sweep"] = c5
         if decode is not None:
@@ -1205,6 +1263,7 @@ def main():
         print(json.dumps(line), flush=True)
     if world > 1:
         reducer.close()
+        split_reducer.close()
         dist.barrier()
         dist.destroy_process_group()
     return 0

@@ -114,7 +114,13 @@ class InprojConvParams(ctypes.Structure):
 
 class PeerReduceParams(ctypes.Structure):
     _fields_ = [("rank", c_i32), ("world", c_i32), ("exchange", c_ptr), ("epochs", c_ptr),
-                ("max_polls", ctypes.c_uint32), ("reserved", ctypes.c_uint32), ("status", c_ptr)]
+                ("max_polls", ctypes.c_uint32), ("flags", ctypes.c_uint32), ("status", c_ptr)]
+
+
+# cc1d_peer_reduce.flags
+PEER_FUSED = 0
+PEER_PUSH = 1
+PEER_FINISH = 2
 
 
 # Every symbol include/cc1d.h declares, with its ctypes signature.

@@ -224,6 +224,7 @@ def _bwd_peer_impl(
     world: int,
     max_polls: int,
     status: torch.Tensor | None,
+    flags: int,
 ) -> None:
     """Backward of a batch shard with dweight/dbias summed over `world` ranks
     in the same kernel (cc1d_bwd_peer_reduce).  exchange_ptrs: int64 device
@@ -231,7 +232,10 @@ def _bwd_peer_impl(
     optional int32 device word, incremented by every wait for a peer that
     gave up (the outputs it could not reduce are written as NaN).
     max_polls (0 = the library default) and status are passed explicitly:
-    a mutated argument of a custom op must be present in every call."""
+    a mutated argument of a custom op must be present in every call.
+    flags: _lib.PEER_FUSED, or PEER_PUSH (backward + push, outputs not
+    written) followed later by PEER_FINISH with the same arguments (only the
+    wait and the outputs; x, dout and dx are not touched)."""
     _require_cuda(x, "causal_conv1d_fn backward (peer reduce)")
     lib = _lib.load()
     p = _bwd_params(x, weight, bias, dout, None, initial_states, dfinal_states, dx, dwdb_acc, dinitial_states,
@@ -240,9 +244,10 @@ def _bwd_peer_impl(
     q.rank, q.world = rank, world
     q.exchange, q.epochs = exchange_ptrs.data_ptr(), epochs.data_ptr()
     q.max_polls = max_polls
+    q.flags = flags
     q.status = _ptr(status)
     with _on_device(x.device):
-        nbytes = bwd_workspace_bytes(p)
+        nbytes = bwd_workspace_bytes(p) if flags != _lib.PEER_FINISH else 0
         ws = None
         if nbytes > 0:
             ws = torch.empty(nbytes, dtype=torch.uint8, device=x.device)
@@ -255,7 +260,7 @@ def _bwd_peer_impl(
 
 def _bwd_peer_fake(x, weight, bias, dout, initial_states, dfinal_states, dx, dwdb_acc, dinitial_states,
                    dweight_out, dbias_out, apply_silu, exchange_ptrs, epochs, rank, world, max_polls,
-                   status) -> None:
+                   status, flags) -> None:
     return None
 
 

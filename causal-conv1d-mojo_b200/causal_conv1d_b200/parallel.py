@@ -102,6 +102,15 @@ class PeerReducer:
     call counters live on the device, so those calls may be captured in a
     CUDA graph and replayed.
 
+    Split exchange: ``args(_lib.PEER_PUSH)`` makes the backward push its
+    sums and return without waiting, and a later call with
+    ``args(_lib.PEER_FINISH)`` and the same tensors -- typically on another
+    stream, so that the wait for the slowest rank overlaps the next work --
+    waits and writes dweight/dbias.  Each FINISH must be ordered before this
+    rank's next PUSH (make the PUSH stream wait on an event recorded after
+    FINISH).  A reducer uses either the fused or the split exchange, not
+    both (the split calls count on their own 4-word counter tensor).
+
     Failure detection: every wait for a peer is bounded (`max_polls` polls,
     0 = the library default of about a second or more).  A wait that gives
     up writes NaN into the gradients it could not reduce and adds 1 to this
@@ -156,6 +165,8 @@ class PeerReducer:
             ptrs[r] = int(mp)
         self.exchange_ptrs = torch.tensor(ptrs, dtype=torch.int64, device=dev)
         self.epochs = torch.zeros(max(self.nblocks, 1), dtype=torch.int32, device=dev)
+        self.split_epochs = torch.zeros(4, dtype=torch.int32, device=dev)
+        self._mode = None
         self.status = torch.zeros(1, dtype=torch.int32, device=dev)
         torch.cuda.synchronize(dev)
         dist.barrier(group=group)
@@ -186,15 +197,28 @@ class PeerReducer:
         self._mapped = []
         self.exchange_ptrs = exchange_ptrs
         self.epochs = torch.zeros(max(self.nblocks, 1), dtype=torch.int32, device=self.device)
+        self.split_epochs = torch.zeros(4, dtype=torch.int32, device=self.device)
+        self._mode = None
         self.status = torch.zeros(1, dtype=torch.int32, device=self.device)
         return self
 
-    def args(self) -> tuple[torch.Tensor, torch.Tensor, int, int, int, torch.Tensor]:
-        """(exchange_ptrs, epochs, rank, world, max_polls, status) for
-        ``_ops.bwd_peer``."""
+    def args(self, flags: int = _lib.PEER_FUSED) -> tuple[torch.Tensor, torch.Tensor, int, int, int, torch.Tensor,
+                                                           int]:
+        """(exchange_ptrs, epochs, rank, world, max_polls, status, flags) for
+        ``_ops.bwd_peer``: the fused exchange (default), or one half of the
+        split exchange (_lib.PEER_PUSH / _lib.PEER_FINISH)."""
         if self._own is None:
             raise RuntimeError("PeerReducer is closed")
-        return self.exchange_ptrs, self.epochs, self.rank, self.world, self.max_polls, self.status
+        if flags not in (_lib.PEER_FUSED, _lib.PEER_PUSH, _lib.PEER_FINISH):
+            raise ValueError(f"unknown peer-exchange flags {flags}")
+        mode = "fused" if flags == _lib.PEER_FUSED else "split"
+        if self._mode is None:
+            self._mode = mode
+        elif self._mode != mode:
+            raise RuntimeError(f"PeerReducer already used for the {self._mode} exchange; the fused and the split "
+                               f"exchange cannot share one reducer")
+        epochs = self.epochs if mode == "fused" else self.split_epochs
+        return self.exchange_ptrs, epochs, self.rank, self.world, self.max_polls, self.status, int(flags)
 
     def failed_waits(self) -> int:
         """Waits for a peer that gave up since the last ``check()`` (reads

@@ -266,18 +266,30 @@ int bwd_impl(const cc1d_bwd_params* p, const cc1d_peer_reduce* peer, void* strea
   int rc = bwd_args(p, &a);
   if (rc) return rc;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const unsigned mode = peer != nullptr ? peer->flags : CC1D_PEER_FUSED;
   if (peer != nullptr) {
     if (peer->world < 1 || peer->rank < 0 || peer->rank >= peer->world || peer->world > 32)
       return fail(CC1D_ERR_INVALID_ARGUMENT, "cc1d_bwd_peer_reduce: rank %d / world %d invalid (world <= 32)",
                   peer->rank, peer->world);
     if (p->dim > 0 && (!peer->exchange || !peer->epochs))
       return fail(CC1D_ERR_INVALID_ARGUMENT, "cc1d_bwd_peer_reduce: exchange and epochs are required");
+    if (mode != CC1D_PEER_FUSED && mode != CC1D_PEER_PUSH && mode != CC1D_PEER_FINISH)
+      return fail(CC1D_ERR_INVALID_ARGUMENT, "cc1d_bwd_peer_reduce: unknown flags %u", mode);
   }
   if (p->dim == 0) return ok();
   if ((rc = bind_device(p->dwdb_acc, "cc1d_bwd")) != CC1D_OK) return rc;
   Plan plan;
   std::memset(&plan, 0, sizeof(plan));
   cudaError_t e = cudaSuccess;
+  if (mode == CC1D_PEER_FINISH) {
+    // Second half of a split exchange: only the wait and the outputs.
+    FinalizeArgs f{nullptr, 0, p->dim, p->dwdb_acc, p->dweight_out, p->dweight_dim_stride, p->dweight_width_stride,
+                   p->dbias_out, p->dbias_stride, p->bias != nullptr ? 1 : 0};
+    PeerFinalizeArgs pf{f, peer->rank, peer->world, peer->exchange, peer->epochs, peer_blocks(p->dim, p->width),
+                        peer->max_polls != 0 ? peer->max_polls : 4194304u, peer->status};
+    e = launch_finalize_peer(p->dtype, p->width, pf, 2, s);
+    return e == cudaSuccess ? ok() : cuda_fail(e, "cc1d_bwd_peer_reduce finish launch");
+  }
   if (p->batch * p->seqlen > 0) {
     const int fam = bwd_family(p->dtype, a);
     e = plan_bwd_any(p->dtype, p->width, a, &plan);
@@ -303,7 +315,7 @@ int bwd_impl(const cc1d_bwd_params* p, const cc1d_peer_reduce* peer, void* strea
   } else {
     PeerFinalizeArgs pf{f, peer->rank, peer->world, peer->exchange, peer->epochs, peer_blocks(p->dim, p->width),
                         peer->max_polls != 0 ? peer->max_polls : 4194304u, peer->status};
-    e = launch_finalize_peer(p->dtype, p->width, pf, s);
+    e = launch_finalize_peer(p->dtype, p->width, pf, mode == CC1D_PEER_PUSH ? 1 : 0, s);
     if (e != cudaSuccess) return cuda_fail(e, "cc1d_bwd_peer_reduce finalize launch");
   }
   return ok();

@@ -148,7 +148,8 @@ cudaError_t read_seq_wait_timeouts(unsigned* count);
 
 i64 peer_blocks(i64 dim, int width);
 i64 peer_exchange_bytes(i64 dim, int width, int world);
-cudaError_t launch_finalize_peer(int dtype, int width, const PeerFinalizeArgs& p, cudaStream_t stream);
+// mode: 0 the fused exchange, 1 push only, 2 finish only (cc1d_peer.cu).
+cudaError_t launch_finalize_peer(int dtype, int width, const PeerFinalizeArgs& p, int mode, cudaStream_t stream);
 cudaError_t read_peer_timeouts(unsigned* count);
 // Blocks of the fused in_proj + conv kernel that gave up on a bounded wait.
 cudaError_t read_fused_aborts(unsigned* count);

@@ -150,13 +150,29 @@ CC1D_API int cc1d_bwd(const cc1d_bwd_params* params, void* stream);
  * dbias_out elements it could not reduce -- never stale values -- adds 1 to
  * *status (when given) and to the count cc1d_device_status reports.  The
  * call numbers still advance, so the ranks stay in step for the next call.
+ *
+ * Split exchange (flags): CC1D_PEER_PUSH runs the backward and the first half
+ * of the reduction only -- the local sums are pushed to every rank and the
+ * call returns without waiting; dwdb_acc / dweight_out / dbias_out are not
+ * written.  A later call with CC1D_PEER_FINISH and the same params (nothing
+ * but the reduction runs: no backward, no workspace) waits for the ranks'
+ * sums and writes the outputs.  Issue FINISH on another stream to overlap the
+ * wait for the slowest rank with other work, and order each FINISH before
+ * the same rank's next PUSH (e.g. the PUSH stream waits on an event recorded
+ * after FINISH).  Split calls count on their own epochs array: 4 zeroed
+ * uint32 words shared by the PUSH and FINISH calls of one reducer, which
+ * must not also make fused calls (flags 0) on the same exchange buffers.
  */
+#define CC1D_PEER_FUSED 0u
+#define CC1D_PEER_PUSH 1u
+#define CC1D_PEER_FINISH 2u
+
 typedef struct cc1d_peer_reduce {
   int32_t rank, world;                 /* world <= 32 */
   unsigned long long* const* exchange; /* device array [world] */
   uint32_t* epochs;                    /* this rank's counters */
   uint32_t max_polls;                  /* polls per wait before giving up; 0 = 4194304 (seconds) */
-  uint32_t reserved;                   /* must be 0 */
+  uint32_t flags;                      /* CC1D_PEER_FUSED (0), CC1D_PEER_PUSH or CC1D_PEER_FINISH */
   uint32_t* status;                    /* device word, or NULL: +1 per wait that gave up (the caller
                                           zeroes it and reads it at a sync point of its choosing) */
 } cc1d_peer_reduce;

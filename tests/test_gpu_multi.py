@@ -159,6 +159,63 @@ def _run_case(case, rank, world, dev):
     finally:
         reducer.close()
 
+    # Split exchange: the backward pushes, a FINISH on a side stream waits
+    # and writes dweight/dbias; each FINISH is ordered before the next PUSH.
+    split = PeerReducer(D, W, dev)
+    try:
+        side = torch.cuda.Stream(dev)
+        dx = torch.empty_like(xs)
+        dwdb = torch.empty(D * (W + 1), dtype=torch.float32, **to)
+        dinit = torch.empty_like(inits)
+        dw = torch.empty(D, W, dtype=dtype, **to)
+        db = torch.empty(D, dtype=dtype, **to) if has_bias else None
+        static_dout = torch.empty_like(douts_s[0])
+
+        def split_call():
+            main = torch.cuda.current_stream(dev)
+            _ops.bwd_peer(xs, ws, bs, static_dout, inits, None, dx, dwdb, dinit, dw, db, True,
+                          *split.args(_lib.PEER_PUSH))
+            pushed = torch.cuda.Event()
+            pushed.record(main)
+            with torch.cuda.stream(side):
+                side.wait_event(pushed)
+                _ops.bwd_peer(xs, ws, bs, static_dout, inits, None, dx, dwdb, dinit, dw, db, True,
+                              *split.args(_lib.PEER_FINISH))
+                done = torch.cuda.Event()
+                done.record(side)
+            main.wait_event(done)
+
+        def check_split(i, how):
+            ref_dx, ref_dinit, total = local(douts_s[i])
+            tag = f"split {how} call {i} rank {rank}"
+            assert torch.equal(dwdb, total), tag
+            assert torch.equal(dw, total[: D * W].view(D, W).to(dtype)), tag
+            if has_bias:
+                assert torch.equal(db, total[D * W:].to(dtype)), tag
+            assert torch.equal(dx, ref_dx), tag
+            assert torch.equal(dinit, ref_dinit), tag
+
+        for i in range(4):
+            static_dout.copy_(douts_s[i])
+            split_call()
+            torch.cuda.synchronize(dev)
+            check_split(i, "eager")
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            split_call()
+        for i in (2, 0, 3, 1):
+            static_dout.copy_(douts_s[i])
+            g.replay()
+            torch.cuda.synchronize(dev)
+            check_split(i, "graph")
+        del g
+        with pytest.raises(RuntimeError, match="cannot share one reducer"):
+            split.args()
+        split.check()
+        assert _lib.device_wait_timeouts() == 0
+    finally:
+        split.close()
+
 
 def _run_dim_shard(rank, world, dev):
     """Dim sharding ('sharded over dim'): rank r runs
@@ -311,7 +368,7 @@ def test_peer_wait_gives_up_and_reports():
     dwdb = torch.full((D * (W + 1),), float("nan"), device=dev)
     dw = torch.full((D, W), float("nan"), dtype=torch.bfloat16, device=dev)
     db = torch.full((D,), float("nan"), dtype=torch.bfloat16, device=dev)
-    _ops.bwd_peer(x, w, b, dout, init, None, dx, dwdb, dinit, dw, db, True, ptrs, epochs, 0, 2, 1024, None)
+    _ops.bwd_peer(x, w, b, dout, init, None, dx, dwdb, dinit, dw, db, True, ptrs, epochs, 0, 2, 1024, None, 0)
     torch.cuda.synchronize(dev)
     assert _lib.device_wait_timeouts() > 0
     assert torch.isnan(dwdb).all() and torch.isnan(dw).all() and torch.isnan(db).all()
@@ -325,7 +382,7 @@ def test_peer_wait_gives_up_and_reports():
     one = torch.zeros_like(own)
     _ops.bwd_peer(x, w, b, dout, init, None, dx, dwdb, dinit, dw, db, True,
                   torch.tensor([one.data_ptr()], dtype=torch.int64, device=dev),
-                  torch.zeros(nblocks, dtype=torch.int32, device=dev), 0, 1, 0, None)
+                  torch.zeros(nblocks, dtype=torch.int32, device=dev), 0, 1, 0, None, 0)
     torch.cuda.synchronize(dev)
     assert _lib.device_wait_timeouts() == 0
     assert torch.equal(dwdb, ref_dwdb)
@@ -365,3 +422,65 @@ def test_batch_sharded_autograd_raises_when_a_peer_never_arrives():
     reducer.check()  # the status word was reset by the failed check
     assert _lib.device_wait_timeouts(dev) > 0
     reducer.close()
+
+
+def test_split_exchange_single_rank_and_bounded_finish():
+    """The split exchange on one GPU: with a world of one, PUSH then FINISH
+    (any streams, in order) gives the local reduction bitwise and writes
+    nothing before FINISH; with a 'peer' that never pushes, the FINISH wait
+    gives up after max_polls, writes NaN, counts the failure in the status
+    word and in cc1d_device_status, and the context stays usable."""
+    from causal_conv1d_b200 import _lib, _ops
+
+    dev = torch.device("cuda", 0)
+    B, D, L, W = 2, 320, 96, 4
+    x, w, b, init, douts = _case_inputs(torch.bfloat16, B, D, L, W, 23, True, True)
+    x, w, b, init, dout = x.to(dev), w.to(dev), b.to(dev), init.to(dev), douts[0].to(dev)
+    lib = _lib.load()
+    nbytes = int(lib.cc1d_peer_exchange_bytes(D, W, 2))
+    ref_dx, ref_dwdb, ref_dinit = torch.empty_like(x), torch.empty(D * (W + 1), device=dev), torch.empty_like(init)
+    _ops.bwd(x, w, b, dout, None, init, None, ref_dx, ref_dwdb, ref_dinit, None, None, True)
+    # World of one.
+    one = torch.zeros(nbytes // 8, dtype=torch.int64, device=dev)
+    ptrs = torch.tensor([one.data_ptr()], dtype=torch.int64, device=dev)
+    ctr = torch.zeros(4, dtype=torch.int32, device=dev)
+    dx, dinit = torch.empty_like(x), torch.empty_like(init)
+    dwdb = torch.full((D * (W + 1),), 7.0, device=dev)
+    dw = torch.full((D, W), 7.0, dtype=torch.bfloat16, device=dev)
+    db = torch.full((D,), 7.0, dtype=torch.bfloat16, device=dev)
+    for call in range(3):
+        _ops.bwd_peer(x, w, b, dout, init, None, dx, dwdb, dinit, dw, db, True, ptrs, ctr, 0, 1, 0, None,
+                      _lib.PEER_PUSH)
+        torch.cuda.synchronize(dev)
+        if call == 0:
+            assert torch.all(dwdb == 7.0)  # PUSH writes no output
+        side = torch.cuda.Stream(dev)
+        with torch.cuda.stream(side):
+            _ops.bwd_peer(x, w, b, dout, init, None, dx, dwdb, dinit, dw, db, True, ptrs, ctr, 0, 1, 0, None,
+                          _lib.PEER_FINISH)
+        torch.cuda.synchronize(dev)
+        assert torch.equal(dwdb, ref_dwdb)
+        assert torch.equal(dw, ref_dwdb[: D * W].view(D, W).to(torch.bfloat16))
+        assert torch.equal(db, ref_dwdb[D * W:].to(torch.bfloat16))
+        assert torch.equal(dx, ref_dx) and torch.equal(dinit, ref_dinit)
+    assert ctr[0].item() == 3 and ctr[2].item() == 3 and ctr[1].item() == 0 and ctr[3].item() == 0
+    assert _lib.device_wait_timeouts() == 0
+    # A world of two whose second rank never pushes.
+    own = torch.zeros(nbytes // 8, dtype=torch.int64, device=dev)
+    silent = torch.zeros_like(own)
+    ptrs2 = torch.tensor([own.data_ptr(), silent.data_ptr()], dtype=torch.int64, device=dev)
+    ctr2 = torch.zeros(4, dtype=torch.int32, device=dev)
+    status = torch.zeros(1, dtype=torch.int32, device=dev)
+    _ops.bwd_peer(x, w, b, dout, init, None, dx, dwdb, dinit, dw, db, True, ptrs2, ctr2, 0, 2, 1024, status,
+                  _lib.PEER_PUSH)
+    _ops.bwd_peer(x, w, b, dout, init, None, dx, dwdb, dinit, dw, db, True, ptrs2, ctr2, 0, 2, 1024, status,
+                  _lib.PEER_FINISH)
+    torch.cuda.synchronize(dev)
+    assert status.item() > 0
+    assert _lib.device_wait_timeouts() > 0
+    assert torch.isnan(dwdb).all() and torch.isnan(dw).all() and torch.isnan(db).all()
+    assert ctr2[0].item() == 1 and ctr2[2].item() == 1
+    # Still usable.
+    _ops.bwd(x, w, b, dout, None, init, None, dx, dwdb, dinit, None, None, True)
+    torch.cuda.synchronize(dev)
+    assert torch.equal(dwdb, ref_dwdb)
