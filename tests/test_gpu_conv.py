@@ -281,6 +281,29 @@ def test_seq_idx_reused_ids_and_step_edges_vs_oracle(dtype, W, layout):
     _compare_oracle(x, w, b, seq, None, dout, None, True, False, layout)
 
 
+@pytest.mark.parametrize("seq", [False, True])
+@pytest.mark.parametrize("W", [2, 4])
+@pytest.mark.parametrize("dtype", ["fp32", "bf16", "fp16"])
+def test_chanlast_odd_dim_vs_oracle(dtype, W, seq):
+    """Channel-last data whose dim is not a multiple of 8 (rows not 16-byte
+    aligned, so neither TMA nor vector loads apply): the register kernels,
+    with a lane's channels 32 apart; several channel groups, the last one
+    ragged, with initial / final states (or seq_idx)."""
+    dt = DTYPES[dtype]
+    B, D, L = 2, 299, 300
+    seed = 31 * D + W + (7 if seq else 0)
+    x = seeded((B, D, L), dt, seed)
+    w = seeded((D, W), dt, seed + 1, "uniform")
+    b = seeded((D,), dt, seed + 2, "uniform")
+    dout = seeded((B, D, L), dt, seed + 4)
+    if seq:
+        _compare_oracle(x, w, b, random_seq_idx(B, L, seed), None, dout, None, True, False, "chanlast")
+    else:
+        init = seeded((B, D, W - 1), dt, seed + 3)
+        dfinal = seeded((B, D, W - 1), dt, seed + 5)
+        _compare_oracle(x, w, b, None, init, dout, dfinal, True, True, "chanlast")
+
+
 @pytest.mark.parametrize("W", [5, 6, 7, 8, 9])
 @pytest.mark.parametrize("layout", ["contig", "chanlast"])
 def test_wide_widths_vs_oracle(W, layout):
