@@ -853,7 +853,7 @@ def time_kernels(peak):
     nbytes = Bu * Du * (2 * Lb + 2 * Lb + 6 + 6) + Du * (W + 1) * 2 + Bu * 4
     res["update_burst4_indexed"] = dict(ms=ms, gbs=nbytes / ms / 1e6, frac=nbytes / ms / 1e6 / peak,
                                         tokens_per_s=Bu * Lb / (ms / 1e3), algorithmic_bytes=nbytes,
-                                        note="x (256, 5376, 4), pool (512, 5376, 3), generic update kernel")
+                                        note="x (256, 5376, 4), pool (512, 5376, 3), update_lin_kernel")
     del xs, pools, outs
     xs = [rn(Bu, Du, 1) for _ in range(sets)]
     pools = [rn(512, W - 1, Du).transpose(1, 2) for _ in range(sets)]
